@@ -1,0 +1,115 @@
+/* mogt_scan.h — C ABI of the B200 (sm_100a) MOGT scan library, libmogt_scan.so.
+ *
+ * The library computes MOGT's affine recurrence H_t = U_t H_{t-1} + V_t and
+ * its headed, gated form
+ *     S_t = f_t S_{t-1} + (1 - f_t) k_t v_t^T,     o_t = S_t^T q_t
+ * (U_t = f_t I, V_t = (1-f_t) k_t v_t^T), forward and backward.
+ *
+ * Conventions shared by every entry point:
+ *   - all tensor pointers are DEVICE pointers of dense, C-contiguous arrays;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every call is
+ *     stream-ordered and asynchronous: no host synchronisation, no allocation;
+ *   - the caller owns every buffer, including the `workspace` whose size the
+ *     matching *_workspace_bytes() returns.  A workspace must be zero-filled
+ *     once before its first use; each call leaves it ready for the next call.
+ *     Calls that share a workspace must not overlap on the GPU (use one
+ *     workspace per stream);
+ *   - return value: MOGT_OK or one of the MOGT_ERR_* codes below.  Kernel-side
+ *     failures (a look-back wait that timed out) are recorded in the
+ *     workspace and read back with mogt_workspace_status().
+ *
+ * The reference (lkcfqy/MOGT) exposes this path as Python functions only; the
+ * comment above each entry point names the reference function it replaces.
+ */
+#ifndef MOGT_SCAN_H_
+#define MOGT_SCAN_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MOGT_ABI_VERSION 1
+
+enum mogt_status {
+  MOGT_OK = 0,
+  MOGT_ERR_SHAPE = 1,       /* bad rank/shape: the reference raises ValueError */
+  MOGT_ERR_DTYPE = 2,       /* unsupported dtype combination */
+  MOGT_ERR_ALIGN = 3,       /* pointer not 16-byte aligned */
+  MOGT_ERR_LAUNCH = 4,      /* CUDA launch / TMA descriptor failure */
+  MOGT_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
+  MOGT_ERR_WORKSPACE = 6,   /* workspace missing or too small */
+  MOGT_ERR_UNSUPPORTED = 7, /* valid request this build does not implement */
+  MOGT_ERR_ARG = 8          /* null pointer where one is required */
+};
+
+enum mogt_dtype { MOGT_DTYPE_F32 = 0, MOGT_DTYPE_BF16 = 1, MOGT_DTYPE_F16 = 2 };
+
+int mogt_abi_version(void);
+const char* mogt_status_string(int status);
+
+/* Copy the workspace's sticky error word to the host (synchronises `stream`).
+ * *err_out = MOGT_OK or MOGT_ERR_TIMEOUT; *unit_out = first failing unit. */
+int mogt_workspace_status(const void* workspace, void* stream, int* err_out, uint32_t* unit_out);
+/* Zero a workspace (first use, or after an error). */
+int mogt_workspace_clear(void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Headed gated scan, forward.  Replaces the composition the reference's MOGT
+ * operator performs for a scalar gate: affine_scan.py:14-62
+ * (affine_scan_sequential with U = f I, V = (1-f) k v^T) followed by the
+ * readout einsum o_t = S_t^T q_t.
+ *
+ *   q, k : [BH, T, dk]   v, o : [BH, T, dv]   f : [BH, T] fp32
+ *   in_dtype  : MOGT_DTYPE_BF16 (tensor-core chunked path, dk = dv = 64) or
+ *               MOGT_DTYPE_F32 (exact fp32 path, dk, dv <= 128)
+ *   out_dtype : dtype of o (MOGT_DTYPE_BF16 or MOGT_DTYPE_F32)
+ *   S0          [BH, dk, dv] fp32 initial state, or NULL for zeros
+ *   S_final     [BH, dk, dv] fp32 final state S_T, or NULL
+ *   decay_final [BH] fp32 product of all f (the carry's decay), or NULL
+ *   seg_states  [BH, nseg, dk, dv] fp32 state entering each segment (saved for
+ *               the backward), or NULL; nseg = mogt_gated_scan_num_segments()
+ *   o may be NULL: only the final state / decay are produced (the first phase
+ *   of the sequence-parallel scan).
+ * Gates must lie in [0, 1] (the chunked path works with log2 f).
+ * ------------------------------------------------------------------------- */
+int64_t mogt_gated_scan_num_segments(int64_t T, int64_t dk, int64_t dv, int in_dtype);
+size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                                           int in_dtype);
+int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
+                        const float* S0, float* S_final, float* decay_final, float* seg_states,
+                        int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).
+ * Replaces triton_scan.py:232-311 (_triton_affine_scan_hybrid_forward: local
+ * Triton kernel + Python carry scan + carry apply), triton_scan.py:151-175
+ * (triton_fused_scan: C = 0, prefix products only) and the reverse scan of
+ * triton_scan.py:398-416 / affine_scan.py:110-118 (reverse != 0).
+ *
+ *   U : [B, L, R, R] (f32 or bf16),  V : [B, L, R, C] (f32 or bf16)
+ *   H : [B, L, R, C] out_dtype, the states H_t; may be NULL when C == 0
+ *   U_prefix : [B, L, R, R] out_dtype, P_t = U_t ... U_0, or NULL
+ *   reverse != 0 computes Sigma_t = V_t + U_{t+1}^T Sigma_{t+1} (the adjoint
+ *   recurrence of the backward, V = grad_H) into H; U_prefix must be NULL.
+ *   R in {2, 4, 8, 16, 32}; C + R <= 512 (R <= 16) or <= 256 (R = 32).
+ * ------------------------------------------------------------------------- */
+size_t mogt_affine_scan_workspace_bytes(int64_t B, int64_t L, int64_t R, int64_t C);
+int mogt_affine_scan_fwd(const void* U, const void* V, void* H, void* U_prefix, int64_t B,
+                         int64_t L, int64_t R, int64_t C, int u_dtype, int v_dtype, int out_dtype,
+                         int reverse, void* workspace, size_t workspace_bytes, void* stream);
+
+/* dU_t = Sigma_t H_{t-1}^T with H_{-1} = 0 (affine_scan.py:117 /
+ * triton_scan.py:421-424).  sigma, H : [B, L, R, C] fp32; grad_U : [B, L, R, R]
+ * in out_dtype. */
+int mogt_affine_grad_u(const float* sigma, const float* H, void* grad_U, int64_t B, int64_t L,
+                       int64_t R, int64_t C, int out_dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOGT_SCAN_H_ */

@@ -1,0 +1,126 @@
+"""ctypes binding of libmogt_scan.so (the C ABI declared in include/mogt_scan.h).
+
+The library is loaded on first use and the product path has no alternative:
+if the shared object is missing, every op raises instead of computing
+anything on the CPU.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmogt_scan.so"
+
+F32, BF16, F16 = 0, 1, 2
+_DT = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
+
+OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_TIMEOUT, ERR_WORKSPACE, ERR_UNSUPPORTED, ERR_ARG = range(9)
+
+_vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/mogt_scan.h
+SIGNATURES = {
+    "mogt_abi_version": (_int, []),
+    "mogt_status_string": (ctypes.c_char_p, [_int]),
+    "mogt_workspace_status": (_int, [_vp, _vp, ctypes.POINTER(_int), ctypes.POINTER(ctypes.c_uint32)]),
+    "mogt_workspace_clear": (_int, [_vp, _sz, _vp]),
+    "mogt_gated_scan_num_segments": (_i64, [_i64, _i64, _i64, _int]),
+    "mogt_gated_scan_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
+    "mogt_gated_scan_fwd": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp, _sz, _vp]),
+    "mogt_affine_scan_workspace_bytes": (_sz, [_i64] * 4),
+    "mogt_affine_scan_fwd": (_int, [_vp] * 4 + [_i64] * 4 + [_int] * 4 + [_vp, _sz, _vp]),
+    "mogt_affine_grad_u": (_int, [_vp] * 3 + [_i64] * 4 + [_int, _vp]),
+}
+
+_lib = None
+_lock = threading.Lock()
+
+
+def lib():
+    """Load libmogt_scan.so (raises if it was not built)."""
+    global _lib
+    if _lib is None:
+        with _lock:
+            if _lib is None:
+                if not LIB_PATH.exists():
+                    raise RuntimeError(
+                        f"{LIB_PATH} is missing: build it with `python -m mogt_b200.build` "
+                        "(the MOGT scan ops have no CPU fallback)")
+                L = ctypes.CDLL(str(LIB_PATH))
+                for name, (res, args) in SIGNATURES.items():
+                    fn = getattr(L, name)
+                    fn.restype = res
+                    fn.argtypes = args
+                if L.mogt_abi_version() != 1:
+                    raise RuntimeError("libmogt_scan.so ABI version mismatch")
+                _lib = L
+    return _lib
+
+
+def dtype_code(dt: torch.dtype) -> int:
+    try:
+        return _DT[dt]
+    except KeyError:
+        raise ValueError(f"unsupported dtype {dt}") from None
+
+
+def check(status: int, what: str) -> None:
+    if status == OK:
+        return
+    msg = lib().mogt_status_string(status).decode()
+    if status in (ERR_SHAPE, ERR_DTYPE, ERR_UNSUPPORTED):
+        raise ValueError(f"{what}: {msg}")
+    raise RuntimeError(f"{what}: {msg} (status {status})")
+
+
+def ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def stream_ptr(device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+class _Workspaces:
+    """One zero-initialised workspace per (device, stream), grown on demand.
+
+    The kernels leave a workspace ready for the next call, so it is zeroed
+    only when (re)allocated.  Calls on one stream are ordered, which is what
+    sharing a workspace requires."""
+
+    def __init__(self):
+        self._ws = {}
+
+    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
+        buf = self._ws.get(key)
+        if buf is None or buf.numel() < nbytes:
+            size = max(nbytes, 0 if buf is None else int(buf.numel() * 1.5))
+            buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
+            self._ws[key] = buf
+        return buf
+
+    def status(self, device: torch.device):
+        """(err, unit) of every workspace on `device` (synchronises)."""
+        out = []
+        for (idx, s), buf in self._ws.items():
+            if idx != device.index:
+                continue
+            err, unit = ctypes.c_int(0), ctypes.c_uint32(0)
+            check(lib().mogt_workspace_status(ptr(buf), ctypes.c_void_p(s), ctypes.byref(err),
+                                              ctypes.byref(unit)), "mogt_workspace_status")
+            out.append((err.value, unit.value))
+        return out
+
+
+workspaces = _Workspaces()
+
+
+def workspace_errors(device=None):
+    """Return the sticky device-side error codes recorded in this process's
+    workspaces on `device` (0 = none).  Synchronises the device."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    return [e for e, _ in workspaces.status(device)]

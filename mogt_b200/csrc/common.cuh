@@ -1,0 +1,242 @@
+// Shared device helpers for the MOGT scan kernels (sm_100a).
+//
+// Everything here is small inline PTX for the data movement and tensor-core
+// primitives the scan kernels use, plus the status codes of the C ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/mogt_scan.h"
+
+namespace mogt {
+
+// Bounded spin: every wait on another CTA's flag or on an mbarrier gives up
+// after this many polls, records MOGT_ERR_TIMEOUT in the workspace header and
+// carries on, so a broken protocol can never hang the GPU.
+constexpr uint32_t kSpinLimit = 1u << 22;
+
+// ----------------------------------------------------------------------------
+// Workspace header of the look-back kernels.  A zero-filled workspace is valid
+// for the first call; each call leaves it valid for the next one (the last CTA
+// to finish resets the ticket and done counters and advances the epoch that
+// tags this call's flags).  err is sticky until the host clears it.
+// ----------------------------------------------------------------------------
+struct WsHeader {
+  uint32_t ticket;
+  uint32_t done;
+  uint32_t epoch;
+  uint32_t err;
+  uint32_t err_unit;
+  uint32_t pad[59];
+};
+static_assert(sizeof(WsHeader) == 256, "header is 256 bytes");
+
+enum : uint32_t { kFlagNone = 0, kFlagAgg = 1, kFlagInc = 2 };
+
+__device__ __forceinline__ uint32_t flag_tag(uint32_t epoch, uint32_t state) {
+  return ((epoch & 0x3FFFFFFFu) << 2) | state;
+}
+
+__device__ __forceinline__ uint32_t ld_acquire_u32(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_u32(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Take a ticket (the scheduling order of look-back units) and read the epoch.
+// Must be called by one thread.
+__device__ __forceinline__ uint32_t take_ticket(WsHeader* h, uint32_t* epoch) {
+  uint32_t t = atomicAdd(&h->ticket, 1u);
+  *epoch = *reinterpret_cast<volatile uint32_t*>(&h->epoch);
+  return t;
+}
+
+// Called by one thread of every CTA at exit: the last CTA re-arms the header.
+__device__ __forceinline__ void finish_cta(WsHeader* h, uint32_t epoch, uint32_t nblocks) {
+  __threadfence();
+  uint32_t prev = atomicAdd(&h->done, 1u);
+  if (prev == nblocks - 1) {
+    h->ticket = 0;
+    h->done = 0;
+    __threadfence();
+    atomicExch(&h->epoch, epoch + 1);
+  }
+}
+
+__device__ __forceinline__ void record_error(WsHeader* h, uint32_t code, uint32_t unit) {
+  if (atomicCAS(&h->err, 0u, code) == 0u) h->err_unit = unit;
+}
+
+// Wait until flags[m] carries this epoch's tag with a state >= AGG.  Returns the
+// state, or kFlagNone after a timeout (which is recorded).
+__device__ __forceinline__ uint32_t wait_flag(const uint32_t* flag, uint32_t epoch, WsHeader* h,
+                                              uint32_t unit) {
+  const uint32_t want = (epoch & 0x3FFFFFFFu);
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    uint32_t v = ld_acquire_u32(flag);
+    if ((v >> 2) == want && (v & 3u) != 0u) return v & 3u;
+    if (it > 64) __nanosleep(it > 4096 ? 256 : 32);
+  }
+  record_error(h, MOGT_ERR_TIMEOUT, unit);
+  return kFlagNone;
+}
+
+// ----------------------------------------------------------------------------
+// Shared-memory / TMA / mbarrier primitives
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// Byte offset of 16-byte chunk `chunk` of row `row` in a tile of 128-byte rows
+// written by TMA with CU_TENSOR_MAP_SWIZZLE_128B (tile base 1024-byte aligned).
+__device__ __forceinline__ uint32_t sw128(uint32_t row, uint32_t chunk) {
+  return row * 128u + ((chunk ^ (row & 7u)) << 4);
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+__device__ __forceinline__ void fence_barrier_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+               "r"(bytes)
+               : "memory");
+}
+
+// Bounded parity wait.  Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
+  const uint32_t addr = smem_u32(bar);
+  for (uint32_t it = 0; it < kSpinLimit; ++it) {
+    uint32_t done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(done)
+        : "r"(addr), "r"(phase)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
+// 3-D tiled TMA load (no multicast) into shared memory, completion counted on
+// `bar` in bytes.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// ----------------------------------------------------------------------------
+// Warp-level tensor-core primitives (bf16 in, fp32 accumulate)
+// ----------------------------------------------------------------------------
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+
+// D += A(16x16, row) * B(16x8, col)
+__device__ __forceinline__ void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+__device__ __forceinline__ float2 unpack_bf16(uint32_t v) {
+  __nv_bfloat162 b = *reinterpret_cast<__nv_bfloat162*>(&v);
+  return __bfloat1622float2(b);
+}
+
+// Multiply both bf16 halves of `v` by (s0, s1) and repack.
+__device__ __forceinline__ uint32_t scale_bf16x2(uint32_t v, float s0, float s1) {
+  float2 f = unpack_bf16(v);
+  return pack_bf16(f.x * s0, f.y * s1);
+}
+
+// PTX approximate base-2 exponent / logarithm (ex2.approx, lg2.approx).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+__device__ __forceinline__ float fast_log2(float x) {
+  float y;
+  asm("lg2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x);
+template <>
+__device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
+template <>
+__device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+
+template <typename T>
+__device__ __forceinline__ T from_f32(float x);
+template <>
+__device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) { return __float2bfloat16_rn(x); }
+template <>
+__device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+
+}  // namespace mogt
+
+// Host-side helpers shared by the entry points.
+namespace mogt_host {
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+inline int launch_status() {
+  cudaError_t e = cudaGetLastError();
+  return e == cudaSuccess ? MOGT_OK : MOGT_ERR_LAUNCH;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t rank, void* base,
+                      const cuuint64_t* dims, const cuuint64_t* strides_bytes, const cuuint32_t* box,
+                      CUtensorMapSwizzle swizzle);
+
+}  // namespace mogt_host

@@ -1,0 +1,133 @@
+"""Tensor-level wrappers over the C ABI (no autograd).
+
+Every function validates shapes the way the reference does (ValueError on bad
+rank/shape, triton_scan.py:193-201), refuses CPU tensors (the reference's
+Triton path raises the same way, triton_scan.py:191-192) and launches on the
+current CUDA stream.  Nothing here computes on the CPU.
+"""
+from __future__ import annotations
+
+import torch
+
+from . import _native as N
+
+__all__ = ["gated_scan_fwd", "affine_scan", "affine_grad_u", "gated_num_segments"]
+
+
+def _require_cuda(*ts, what):
+    for t in ts:
+        if t is not None and t.device.type != "cuda":
+            raise ValueError(f"{what} requires CUDA tensors")
+
+
+def gated_num_segments(T: int, dk: int, dv: int, dtype: torch.dtype) -> int:
+    return int(N.lib().mogt_gated_scan_num_segments(T, dk, dv, N.dtype_code(dtype)))
+
+
+def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False,
+                   save_states=False, want_output=True):
+    """o_t = S_t^T q_t with S_t = f_t S_{t-1} + (1-f_t) k_t v_t^T.
+
+    q, k: [B, H, T, dk]; v: [B, H, T, dv]; f: [B, H, T] (any float dtype, used
+    as fp32).  bf16 inputs take the tensor-core path (dk = dv = 64); fp32
+    inputs take the exact sequential path.  Returns (o, S_final, decay_final,
+    seg_states) with the optional members None unless requested.
+    """
+    _require_cuda(q, k, v, f, initial_state, what="gated_scan")
+    if k.ndim != 4 or v.ndim != 4 or f.ndim != 3 or (q is not None and q.ndim != 4):
+        raise ValueError("q, k, v must be [B, H, T, d] and f must be [B, H, T]")
+    B, H, T, dk = k.shape
+    dv = v.shape[-1]
+    if v.shape[:3] != (B, H, T) or f.shape != (B, H, T) or (q is not None and q.shape != k.shape):
+        raise ValueError("q, k must be [B, H, T, dk], v [B, H, T, dv], f [B, H, T]")
+    in_dtype = k.dtype
+    if v.dtype != in_dtype or (q is not None and q.dtype != in_dtype):
+        raise ValueError("q, k, v must share one dtype")
+    if in_dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("q, k, v must be bfloat16 or float32")
+    out_dtype = output_dtype or in_dtype
+    dev = k.device
+    k = k.contiguous()
+    v = v.contiguous()
+    q = q.contiguous() if q is not None else None
+    f = f.to(torch.float32).contiguous()
+    BH = B * H
+    o = torch.empty(B, H, T, dv, dtype=out_dtype, device=dev) if want_output else None
+    S0 = None
+    if initial_state is not None:
+        if initial_state.shape != (B, H, dk, dv):
+            raise ValueError("initial_state must be [B, H, dk, dv]")
+        S0 = initial_state.to(torch.float32).contiguous()
+    S_fin = torch.empty(B, H, dk, dv, dtype=torch.float32, device=dev) if want_final else None
+    dec = torch.empty(B, H, dtype=torch.float32, device=dev) if want_final else None
+    seg = None
+    if save_states:
+        nseg = gated_num_segments(T, dk, dv, in_dtype)
+        if nseg > 0:
+            seg = torch.empty(B, H, nseg, dk, dv, dtype=torch.float32, device=dev)
+    L = N.lib()
+    icode, ocode = N.dtype_code(in_dtype), N.dtype_code(out_dtype)
+    nbytes = L.mogt_gated_scan_fwd_workspace_bytes(BH, T, dk, dv, icode)
+    with torch.cuda.device(dev):
+        ws = N.workspaces.get(dev, nbytes)
+        st = L.mogt_gated_scan_fwd(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o), N.ptr(S0),
+                                   N.ptr(S_fin), N.ptr(dec), N.ptr(seg), BH, T, dk, dv, icode, ocode,
+                                   N.ptr(ws), ws.numel(), N.stream_ptr(dev))
+    N.check(st, "mogt_gated_scan_fwd")
+    return o, S_fin, dec, seg
+
+
+def _check_uv(U, V):
+    if U.ndim != 4 or V.ndim != 4:
+        raise ValueError("U and V must be rank-4 tensors")
+    B, L, R, R2 = U.shape
+    Bv, Lv, Rv, C = V.shape
+    if (B, L, R) != (Bv, Lv, Rv) or R != R2:
+        raise ValueError("U must be [B, L, R, R] and V must be [B, L, R, C]")
+    return B, L, R, C
+
+
+def affine_scan(U, V, *, output_dtype=torch.float32, return_prefix=False, reverse=False):
+    """H_t = U_t H_{t-1} + V_t (fp32 state), optionally with the prefix products
+    P_t = U_t ... U_0.  reverse=True computes the backward's adjoint
+    Sigma_t = V_t + U_{t+1}^T Sigma_{t+1}.  V may be None for prefix-only."""
+    _require_cuda(U, V, what="affine_scan")
+    if V is None:
+        if U.ndim != 4 or U.shape[-1] != U.shape[-2]:
+            raise ValueError("U must be [B, L, R, R]")
+        B, L, R, _ = U.shape
+        C = 0
+    else:
+        B, L, R, C = _check_uv(U, V)
+    if U.dtype not in (torch.float32, torch.bfloat16) or (V is not None and V.dtype not in (torch.float32, torch.bfloat16)):
+        raise ValueError("U and V must be float32 or bfloat16")
+    dev = U.device
+    U = U.contiguous()
+    V = V.contiguous() if V is not None else None
+    H = torch.empty(B, L, R, C, dtype=output_dtype, device=dev) if C > 0 else None
+    P = torch.empty(B, L, R, R, dtype=output_dtype, device=dev) if return_prefix else None
+    Lb = N.lib()
+    nbytes = Lb.mogt_affine_scan_workspace_bytes(B, L, R, C)
+    with torch.cuda.device(dev):
+        ws = N.workspaces.get(dev, nbytes)
+        st = Lb.mogt_affine_scan_fwd(N.ptr(U), N.ptr(V), N.ptr(H), N.ptr(P), B, L, R, C,
+                                     N.dtype_code(U.dtype),
+                                     N.dtype_code(V.dtype) if V is not None else N.dtype_code(U.dtype),
+                                     N.dtype_code(output_dtype), int(reverse), N.ptr(ws), ws.numel(),
+                                     N.stream_ptr(dev))
+    N.check(st, "mogt_affine_scan_fwd")
+    return H, P
+
+
+def affine_grad_u(sigma, H, *, output_dtype=torch.float32):
+    """dU_t = Sigma_t H_{t-1}^T (H_{-1} = 0); sigma, H fp32 [B, L, R, C]."""
+    _require_cuda(sigma, H, what="affine_grad_u")
+    B, L, R, C = sigma.shape
+    sigma = sigma.to(torch.float32).contiguous()
+    H = H.to(torch.float32).contiguous()
+    gU = torch.empty(B, L, R, R, dtype=output_dtype, device=sigma.device)
+    with torch.cuda.device(sigma.device):
+        st = N.lib().mogt_affine_grad_u(N.ptr(sigma), N.ptr(H), N.ptr(gU), B, L, R, C,
+                                        N.dtype_code(output_dtype), N.stream_ptr(sigma.device))
+    N.check(st, "mogt_affine_grad_u")
+    return gU

@@ -1,0 +1,136 @@
+"""Gated (headed) scan forward on the GPU vs the oracle.
+
+Tolerances (north star): fp32 inputs <= 1e-4 relative; bf16 inputs with fp32
+accumulation <= 2e-2 relative (max-abs error over max-abs reference)."""
+import numpy as np
+import pytest
+import torch
+
+from oracle import scan_oracle as O
+from tests.golden.make_golden import headed_inputs
+from tests.helpers import as64, headed_bf16, rel_fro_err, rel_max_err
+
+pytestmark = pytest.mark.gpu
+TOL_F32 = 1e-4
+TOL_BF16 = 2e-2
+
+
+@pytest.fixture(scope="module")
+def mg():
+    import mogt_b200
+    from mogt_b200 import _native
+    assert torch.cuda.is_available()
+    return mogt_b200, _native
+
+
+def test_config1_fp32_golden(mg, golden):
+    m, _ = mg
+    d = golden("config1_fp32")
+    q, k, v, f, g = headed_inputs(2, 4, 512, 32, 32, torch.float32)
+    o = m.gated_scan(q.cuda(), k.cuda(), v.cuda(), f.cuda())
+    assert o.dtype == torch.float32
+    assert rel_max_err(o.cpu().numpy(), d["o"]) <= TOL_F32
+
+
+@pytest.mark.parametrize("T", [1, 17, 64, 255, 256, 257, 700, 2048])
+def test_bf16_matches_oracle(mg, T):
+    m, N = mg
+    q, k, v, f = headed_bf16(1, 3, T, seed=T)
+    o = m.gated_scan(q.cuda(), k.cuda(), v.cuda(), f.cuda())
+    assert o.dtype == torch.bfloat16 and o.shape == (1, 3, T, 64)
+    ref = O.gated_scan(*as64(q, k, v, f))
+    assert rel_max_err(o.float().cpu().numpy(), ref) <= TOL_BF16
+    assert rel_fro_err(o.float().cpu().numpy(), ref) <= 5e-3
+    assert all(e == 0 for e in N.workspace_errors())
+
+
+@pytest.mark.parametrize("mode", ["ones", "zeros", "mixed"])
+def test_bf16_gate_edge_cases(mg, mode):
+    m, _ = mg
+    q, k, v, f = headed_bf16(2, 2, 600, seed=5, f_mode=mode)
+    S0 = torch.randn(2, 2, 64, 64)
+    o, S_fin, dec, _ = m.ops.gated_scan_fwd(q.cuda(), k.cuda(), v.cuda(), f.cuda(),
+                                            initial_state=S0.cuda(), output_dtype=torch.float32,
+                                            want_final=True)
+    ref, Sref = O.gated_scan(*as64(q, k, v, f), S0=S0.double().numpy(), return_final=True)
+    assert rel_max_err(o.cpu().numpy(), ref) <= TOL_BF16
+    assert rel_max_err(S_fin.cpu().numpy(), Sref) <= TOL_BF16
+    dref = np.prod(f.double().numpy(), axis=-1)
+    assert np.allclose(dec.cpu().numpy(), dref, rtol=1e-3, atol=1e-30)
+
+
+def test_fp32_initial_and_final_state(mg):
+    m, _ = mg
+    q, k, v, f, _ = headed_inputs(1, 2, 300, 48, 40, torch.float32)
+    S0 = torch.randn(1, 2, 48, 40)
+    o, S_fin, dec, _ = m.ops.gated_scan_fwd(q.cuda(), k.cuda(), v.cuda(), f.cuda(),
+                                            initial_state=S0.cuda(), want_final=True)
+    ref, Sref = O.gated_scan(*as64(q, k, v, f), S0=S0.double().numpy(), return_final=True)
+    assert rel_max_err(o.cpu().numpy(), ref) <= TOL_F32
+    assert rel_max_err(S_fin.cpu().numpy(), Sref) <= TOL_F32
+
+
+def test_segment_states_and_state_only_mode(mg):
+    m, _ = mg
+    T = 1100
+    q, k, v, f = headed_bf16(1, 2, T, seed=11)
+    o, S_fin, dec, seg = m.ops.gated_scan_fwd(q.cuda(), k.cuda(), v.cuda(), f.cuda(),
+                                              want_final=True, save_states=True)
+    assert seg.shape == (1, 2, 5, 64, 64)
+    # state entering segment s is S_{256 s - 1}
+    kk, vv, ff = as64(k, v, f)
+    S = np.zeros((2, 64, 64))
+    assert float(seg[0, :, 0].abs().max()) == 0.0
+    for t in range(T):
+        if t % 256 == 0 and t > 0:
+            assert rel_max_err(seg[0, :, t // 256].cpu().numpy(), S) <= TOL_BF16
+        S = ff[0, :, t, None, None] * S + (1 - ff[0, :, t, None, None]) * kk[0, :, t, :, None] * vv[0, :, t, None, :]
+    assert rel_max_err(S_fin[0].cpu().numpy(), S) <= TOL_BF16
+    # state-only (first phase of the sequence-parallel scan): no q, no o
+    _, S2, dec2, _ = m.ops.gated_scan_fwd(None, k.cuda(), v.cuda(), f.cuda(), want_final=True,
+                                          want_output=False)
+    assert torch.allclose(S2, S_fin, rtol=1e-5, atol=1e-6)
+    assert torch.allclose(dec2, dec)
+
+
+def test_repeated_calls_reuse_workspace(mg):
+    m, N = mg
+    q, k, v, f = (t.cuda() for t in headed_bf16(1, 4, 3000, seed=2))
+    outs = [m.gated_scan(q, k, v, f) for _ in range(4)]
+    for o in outs[1:]:
+        assert torch.equal(o, outs[0])
+    assert all(e == 0 for e in N.workspace_errors())
+
+
+def test_full_length_split_consistency(mg):
+    """Config 2 at full length: scanning [0, T) equals scanning [0, T/2) then
+    [T/2, T) from the carried state (a size-independent property), and the
+    first 2048 steps match the oracle."""
+    m, _ = mg
+    T = 32768
+    q, k, v, f = (t.cuda() for t in headed_bf16(1, 12, T, seed=3))
+    o = m.gated_scan(q, k, v, f, output_dtype=torch.float32)
+    # split at a chunk boundary: identical chunking on both sides, so only the
+    # carry path differs (fp32 sums in another order)
+    h = T // 2 + 64 * 7
+    o1, S1, _, _ = m.ops.gated_scan_fwd(q[:, :, :h], k[:, :, :h], v[:, :, :h], f[:, :, :h],
+                                        output_dtype=torch.float32, want_final=True)
+    o2, _, _, _ = m.ops.gated_scan_fwd(q[:, :, h:], k[:, :, h:], v[:, :, h:], f[:, :, h:],
+                                       initial_state=S1, output_dtype=torch.float32)
+    both = torch.cat([o1, o2], 2)
+    err = (both - o).abs().max() / o.abs().max()
+    assert float(err) <= 2e-3
+    ref = O.gated_scan(*as64(q[:1, :2, :2048], k[:1, :2, :2048], v[:1, :2, :2048], f[:1, :2, :2048]))
+    assert rel_max_err(o[:1, :2, :2048].cpu().numpy(), ref) <= TOL_BF16
+    assert torch.isfinite(o).all()
+
+
+def test_errors(mg):
+    m, _ = mg
+    q, k, v, f = headed_bf16(1, 1, 16)
+    with pytest.raises(ValueError):
+        m.gated_scan(q, k, v, f)  # CPU tensors: no fallback
+    with pytest.raises(ValueError):
+        m.gated_scan(q.cuda()[..., :32], k.cuda()[..., :32], v.cuda()[..., :32], f.cuda())
+    with pytest.raises(ValueError):
+        m.gated_scan(q.cuda(), k.cuda(), v.cuda(), f.cuda()[..., :8])
