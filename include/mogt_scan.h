@@ -42,7 +42,9 @@ enum mogt_status {
   MOGT_ERR_TIMEOUT = 5,     /* a bounded device-side wait gave up */
   MOGT_ERR_WORKSPACE = 6,   /* workspace missing or too small */
   MOGT_ERR_UNSUPPORTED = 7, /* valid request this build does not implement */
-  MOGT_ERR_ARG = 8          /* null pointer where one is required */
+  MOGT_ERR_ARG = 8,         /* null pointer where one is required */
+  MOGT_ERR_TOO_LARGE = 9    /* problem needs more scratch than the fixed
+                               buffer of mogt_gated_scan_fwd_noalloc */
 };
 
 enum mogt_dtype { MOGT_DTYPE_F32 = 0, MOGT_DTYPE_BF16 = 1, MOGT_DTYPE_F16 = 2 };
@@ -82,6 +84,27 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
                         const float* S0, float* S_final, float* decay_final, float* seg_states,
                         int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
+
+/* Allocation-free variant of mogt_gated_scan_fwd.  This entry point has no
+ * counterpart in the reference.  It exists for callers that cannot allocate
+ * device memory: hosts whose device memory is owned by an allocator or a
+ * budget this library cannot reach through a C ABI (a runtime that reserves
+ * all of its GPU memory up front, a foreign-language binding without access
+ * to the caller's allocator), and code that must not pay the implicit device
+ * synchronisation of cudaMalloc/cudaFree.  Arguments and results are those
+ * of mogt_gated_scan_fwd minus the workspace: the scan's scratch lives in a
+ * 16 MiB array built into the library, which every GPU that loads the library
+ * keeps for the life of the process (enough for BASELINE-sized problems such
+ * as 12 heads x 32768 steps; larger requests return MOGT_ERR_TOO_LARGE and
+ * do nothing).  The first call on a device looks up that device's copy of
+ * the array (make it before any stream capture); no call allocates.  All
+ * calls share the one array and each call clears the part that must start
+ * at zero, so calls whose GPU work overlaps (other streams, other host
+ * threads) race and must be serialised by the caller. */
+int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v, const float* f,
+                                void* o, const float* S0, float* S_final, float* decay_final,
+                                float* seg_states, int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                                int in_dtype, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).

@@ -17,7 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmogt_scan.so"
 F32, BF16, F16 = 0, 1, 2
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
-OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_TIMEOUT, ERR_WORKSPACE, ERR_UNSUPPORTED, ERR_ARG = range(9)
+OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_TIMEOUT, ERR_WORKSPACE, ERR_UNSUPPORTED, ERR_ARG, ERR_TOO_LARGE = range(10)
 
 _vp, _i64, _int, _sz = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int, ctypes.c_size_t
 
@@ -30,6 +30,7 @@ SIGNATURES = {
     "mogt_gated_scan_num_segments": (_i64, [_i64, _i64, _i64, _int]),
     "mogt_gated_scan_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
     "mogt_gated_scan_fwd": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp, _sz, _vp]),
+    "mogt_gated_scan_fwd_noalloc": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp]),
     "mogt_affine_scan_workspace_bytes": (_sz, [_i64] * 4),
     "mogt_affine_scan_fwd": (_int, [_vp] * 4 + [_i64] * 4 + [_int] * 4 + [_vp, _sz, _vp]),
     "mogt_affine_grad_u": (_int, [_vp] * 3 + [_i64] * 4 + [_int, _vp]),

@@ -44,6 +44,7 @@ const char* mogt_status_string(int status) {
     case MOGT_ERR_WORKSPACE: return "workspace missing or too small";
     case MOGT_ERR_UNSUPPORTED: return "unsupported configuration";
     case MOGT_ERR_ARG: return "null pointer argument";
+    case MOGT_ERR_TOO_LARGE: return "problem exceeds the fixed 16 MiB scratch of the allocation-free entry point";
     default: return "unknown status";
   }
 }

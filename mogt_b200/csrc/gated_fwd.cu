@@ -632,3 +632,61 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.  Its scratch is a fixed array in the library's
+// device image instead of a caller-provided workspace, for callers that
+// cannot allocate device memory.  The kernel and its arguments are exactly
+// those of mogt_gated_scan_fwd.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(16) << 20;  // 16 MiB per device
+static __device__ __align__(256) uint8_t g_static_scratch[kStaticScratchBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_scratch_mu;
+void* g_scratch_addr[kMaxDevices] = {};
+
+// Device address of this device's copy of g_static_scratch.  In host code the
+// symbol is only a host-side stand-in, so the address is looked up once per
+// device with that device current.  Returns nullptr on failure.
+void* static_scratch_for_current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_scratch_mu);
+  if (!g_scratch_addr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_static_scratch) != cudaSuccess) return nullptr;
+    g_scratch_addr[dev] = p;
+  }
+  return g_scratch_addr[dev];
+}
+
+}  // namespace
+
+extern "C" int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v,
+                                           const float* f, void* o, const float* S0,
+                                           float* S_final, float* decay_final, float* seg_states,
+                                           int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                                           int in_dtype, int out_dtype, void* stream) {
+  if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
+  if (T == 0) return MOGT_OK;
+  size_t clear_bytes = 0;
+  if (in_dtype == MOGT_DTYPE_BF16 && dk == D && dv == D) {
+    if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
+    const Plan pl = make_plan(BH, T, resident_ctas());
+    const WsLayout L = ws_layout((size_t)BH * pl.nstripes);
+    if (L.total > kStaticScratchBytes) return MOGT_ERR_TOO_LARGE;
+    clear_bytes = L.st_agg;  // header, flags and decays must start at zero
+  }
+  void* scratch = static_scratch_for_current_device();
+  if (!scratch) return MOGT_ERR_LAUNCH;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (clear_bytes && cudaMemsetAsync(scratch, 0, clear_bytes, s) != cudaSuccess)
+    return MOGT_ERR_LAUNCH;
+  return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, seg_states, BH, T, dk, dv,
+                             in_dtype, out_dtype, scratch, kStaticScratchBytes, stream);
+}
