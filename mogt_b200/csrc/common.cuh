@@ -240,3 +240,98 @@ CUresult encode_tiled(CUtensorMap* map, CUtensorMapDataType dtype, cuuint32_t ra
                       CUtensorMapSwizzle swizzle);
 
 }  // namespace mogt_host
+
+// ----------------------------------------------------------------------------
+// tcgen05 (5th-generation tensor core) helpers: shared-memory matrix
+// descriptors for 128B-swizzled bf16 tiles of 64-element (128-byte) rows,
+// single-thread MMA issue into tensor memory, completion through an mbarrier,
+// and warp-wide tensor-memory loads in the m16n8 fragment layout.
+// ----------------------------------------------------------------------------
+namespace mogt {
+
+// K-major operand: rows are M (or N), 64 K-elements per 128-byte row, 8-row
+// swizzle atoms of 1024 bytes.  A K=16 step advances the start by 32 bytes.
+__device__ __forceinline__ uint64_t umma_desc_kmajor(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)1 << 16) | ((uint64_t)(1024 >> 4) << 32) |
+         ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// MN-major operand: rows are K, 64 M/N-elements per 128-byte row; groups of 8
+// K-rows are 1024 bytes apart.  A K=16 step advances the start by 2048 bytes.
+__device__ __forceinline__ uint64_t umma_desc_mnmajor(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFF) | ((uint64_t)(8192 >> 4) << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+// Instruction descriptor: kind::f16, bf16 x bf16 -> f32, M = 64, N = 64.
+constexpr uint32_t kIdescBase = (1u << 4) | (1u << 7) | (1u << 10) | ((64u >> 3) << 17) | ((64u >> 4) << 24);
+constexpr uint32_t kIdescAmn = 1u << 15;  // A is MN-major
+constexpr uint32_t kIdescBmn = 1u << 16;  // B is MN-major
+
+__device__ __forceinline__ void umma_bf16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
+                                          uint32_t idesc, bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"((uint32_t)accumulate));
+}
+
+// D(64x64, f32, TMEM) (+)= A(64x64) * B(64x64): four K=16 steps; the first
+// step accumulates onto D only when `accumulate` is set.  The descriptors are
+// built once; a K step only adds to the 14-bit start-address field (shared
+// memory addresses stay below 256 KB, so the field never carries).
+__device__ __forceinline__ void umma_64x64x64(uint32_t d_tmem, uint32_t a_saddr, bool a_mn,
+                                              uint32_t b_saddr, bool b_mn, bool accumulate) {
+  const uint32_t idesc = kIdescBase | (a_mn ? kIdescAmn : 0u) | (b_mn ? kIdescBmn : 0u);
+  const uint64_t ad0 = a_mn ? umma_desc_mnmajor(a_saddr) : umma_desc_kmajor(a_saddr);
+  const uint64_t bd0 = b_mn ? umma_desc_mnmajor(b_saddr) : umma_desc_kmajor(b_saddr);
+  const uint64_t astep = a_mn ? (2048 >> 4) : (32 >> 4);
+  const uint64_t bstep = b_mn ? (2048 >> 4) : (32 >> 4);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk)
+    umma_bf16(d_tmem, ad0 + astep * kk, bd0 + bstep * kk, idesc, accumulate || kk > 0);
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// Warp-wide: 16 rows x 32 f32 columns of an M=64 accumulator (lane field of
+// taddr = 32 * (warp % 4)), in the m16n8 fragment layout acc[n][e]: rows g,
+// g+8 and columns 8n + 2c, +1 of the 32-column slice.
+__device__ __forceinline__ void tmem_ld_16x32(float (&acc)[4][4], uint32_t taddr) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(r[4 * n + e]);
+}
+
+// Tensor-memory allocation by one full warp; the address lands in *slot.
+__device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+               "r"(ncols)
+               : "memory");
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+
+}  // namespace mogt

@@ -5,18 +5,32 @@
 //
 // Work decomposition ("stripes"): the T tokens of every (batch, head) are cut
 // into 64-token chunks and the chunks into a few contiguous stripes, so that
-// BH x stripes ~ one wave of resident CTAs.  A CTA owns one stripe:
-//   pass 1  streams K, V chunks (TMA, 5-stage ring, L2 evict-last) and builds
-//           the stripe's aggregate state  sum_s decay(s->end) (1-f_s) k_s v_s^T
-//           with tensor-core GEMMs (K~^T V per chunk), then publishes it;
+// BH x stripes ~ one wave of resident CTAs.  A CTA (8 warps) owns one stripe:
+//   pass 1  streams K, V chunks (TMA, 5-slot ring, L2 evict-last) and
+//           accumulates the stripe's aggregate state
+//               sum_s decay(s -> stripe end) (1 - f_s) k_s v_s^T
+//           directly in tensor memory: chunk c's K rows are pre-scaled by
+//           their decay to the stripe end, so no per-chunk read-back is needed;
 //   look-back  a windowed decoupled look-back over the earlier stripes of the
 //           same head yields the fp32 state entering the stripe; the stripe's
 //           inclusive state is published for its successors;
-//   pass 2  streams Q, K, V chunks again (3-stage ring, K, V mostly from L2)
+//   pass 2  streams Q, K, V chunks again (3-slot ring, K, V mostly from L2)
 //           and per chunk computes o = diag(a) Q S + ((Q K^T) o D) V and the
-//           state update S <- a_C S + K~^T V (mma.sync bf16 -> fp32).
-// Decays come from chunk-local inclusive log2 cumulative gates: D[t,s] =
-// exp2(l_t - l_s) for s <= t, a_t = exp2(l_t), and per-step log2 gates are
+//           state update S <- a_C S + K~^T V.
+// Tensor cores: every 64x64x64 product is a tcgen05.mma (kind::f16, bf16 ->
+// fp32) issued by one thread from 128B-swizzled shared-memory tiles into
+// tensor memory; the warps read accumulators back with tcgen05.ld, apply
+// the causal mask (and exact decays when needed), and write the bf16
+// operands of the next products.  Pass 2 is software-pipelined: the
+// state-independent products of chunk c+1 run while chunk c is finished.
+// Warp w owns rows 16(w%4)..+15 and columns 32(w/4)..+31 of every 64x64
+// accumulator, and every warp derives the gate values it needs itself.
+// Decays: chunk-local inclusive log2 cumulative gates l_t, D[t,s] =
+// exp2(l_t - l_s) for s <= t.  When the chunk's total decay is above 2^-100
+// the decay factorises, D[t,s] (1-f_s) = exp2(l_t) * [(1-f_s) exp2(-l_s)]:
+// with Q^ = diag(exp2 l) Q and K~ = diag((1-f) exp2(-l)) K, P' is the
+// causally masked Q^ K~^T and o = Q^ S + P' V; otherwise the exact
+// per-element form is used.  Per-step log2 gates are
 // clamped at -64 so f = 0 is a (numerically) full reset.
 #include "common.cuh"
 #include "gated_internal.h"
@@ -24,17 +38,24 @@
 
 #ifdef MOGT_TRACE
 // Debug-only phase timestamps (built into a separate trace library, never
-// into the product): trace[unit * 8 + k] = %globaltimer at phase k.
+// into the product): trace[unit * 16 + k] = %globaltimer at phase k.
 __device__ unsigned long long* g_mogt_trace = nullptr;
 __device__ __forceinline__ void trace_mark(uint32_t unit, int k) {
   unsigned long long t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  if (g_mogt_trace) g_mogt_trace[unit * 8 + k] = t;
+  if (g_mogt_trace) g_mogt_trace[unit * 16 + k] = t;
 }
 #define MOGT_MARK(u, k) \
   if (threadIdx.x == 0) trace_mark(u, k)
+// cycle-resolution marks (SM clock), for sub-phases within one CTA
+__device__ __forceinline__ void trace_clk(uint32_t unit, int k) {
+  if (g_mogt_trace) g_mogt_trace[unit * 16 + k] = clock64();
+}
+#define MOGT_CLK(u, k, cond) \
+  if (threadIdx.x == 0 && (cond)) trace_clk(u, k)
 #else
 #define MOGT_MARK(u, k)
+#define MOGT_CLK(u, k, cond)
 #endif
 
 namespace mogt {
@@ -42,31 +63,37 @@ namespace gated {
 
 constexpr int D = 64;
 constexpr int CH = 64;
-constexpr int NTHREADS = 128;
+constexpr int NTHREADS = 256;             // 8 warps
 constexpr int STAGES = 3;                 // pass-2 ring: q, k, v per slot
 constexpr int P1_STAGES = 5;              // pass-1 ring: k, v per slot
+constexpr int P1_AHEAD = 3;               // pass-1 chunks loading ahead
 constexpr int SEG_CHUNKS = 4;             // saved-state granularity: 256 tokens
+constexpr int MAX_CPS = 256;              // chunks per stripe (suffix table)
 constexpr int TILE = CH * D * 2;          // one 64x64 bf16 tile, 8 KB
 constexpr int SLOT = 3 * TILE;            // q, k, v of one chunk
-
-struct GateBuf {
-  float lg[CH];  // chunk-local inclusive log2 cumulative gate
-  float ck[CH];  // (1 - f_s) * decay(s -> chunk end)
-  float ea[CH];  // decay(chunk start -> t)
-  float wv[CH];  // 1 - f_s
-  float lgC;     // log2 decay of the whole chunk
-  float pad[3];
-};
+constexpr float kFactorMin = -100.f;      // log2 chunk decay above which D factorises
 
 constexpr int SM_RING = 0;
-constexpr int SM_SBUF = SM_RING + STAGES * SLOT;   // 2 x bf16 state operand
-constexpr int SM_GATE = SM_SBUF + 2 * TILE;        // 2 x GateBuf
-constexpr int SM_MISC = SM_GATE + 2 * (int)sizeof(GateBuf);
-constexpr int SM_BAR = SM_MISC + 256;      // STAGES pass-2 + P1_STAGES pass-1 mbarriers
-constexpr int SM_TOTAL = SM_BAR + 8 * (STAGES + P1_STAGES);
-// pass 1 reuses the ring and the state-operand buffers as a deeper k/v ring
-static_assert(P1_STAGES * 2 * TILE <= SM_GATE - SM_RING, "pass-1 ring fits");
+constexpr int SM_SBUF = SM_RING + STAGES * SLOT;   // bf16 state operand [i][j] (+ pass-1 ring)
+constexpr int SM_KT = SM_SBUF + TILE;              // scaled K, [s][i]
+constexpr int SM_QT = SM_KT + TILE;                // scaled Q, [t][i]
+constexpr int SM_PT = SM_QT + TILE;                // masked, decayed P, [t][s]
+constexpr int SM_LSUF = SM_PT + TILE;              // pass-1 suffix decays
+constexpr int SM_MISC = SM_LSUF + MAX_CPS * 4;
+constexpr int NBARS = STAGES + P1_STAGES + 5;      // TMA rings, 2 pass-1 + 3 pass-2 MMA barriers
+constexpr int SM_BAR = SM_MISC + 256;
+constexpr int SM_TSLOT = SM_BAR + 8 * NBARS;
+constexpr int SM_TOTAL = SM_TSLOT + 16;
+// pass 1 reuses the q/k/v ring and the state-operand tile as a deeper k/v
+// ring, and the scaled-K and scaled-Q tiles as a double-buffered scaled K;
+// 2 CTAs per SM must fit
+static_assert(2 * (SM_TOTAL + 1024 + 1024) <= 228 * 1024, "two CTAs per SM");
+static_assert(P1_STAGES * 2 * TILE <= SM_KT - SM_RING, "pass-1 ring fits");
 constexpr int SM_ALLOC = SM_TOTAL + 1024;
+// tensor-memory columns (fp32, M = 64 accumulators in lanes 32q..32q+15):
+// P, K~^T V and a double-buffered O (pass 2); pass 1 accumulates in TM_DS
+constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TM_P = 0, TM_DS = 64, TM_O0 = 128;
 
 struct Params {
   const float* f;
@@ -107,6 +134,9 @@ inline Plan make_plan(int64_t BH, int64_t T, int resident) {
   int64_t sph = BH >= resident ? 1 : resident / BH;
   if (sph > p.nchunks) sph = p.nchunks;
   if (sph < 1) sph = 1;
+  // bound the stripe length (suffix-decay table)
+  const int64_t min_sph = (p.nchunks + MAX_CPS - 1) / MAX_CPS;
+  if (sph < min_sph) sph = min_sph;
   p.cps = (int)((p.nchunks + sph - 1) / sph);
   p.nstripes = (p.nchunks + p.cps - 1) / p.cps;
   return p;
@@ -128,9 +158,10 @@ __device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* m
       : "memory");
 }
 
-// Gates of chunk gc for one warp: lane l holds steps 2l, 2l+1 (t >= T reads
-// as "no step": f = 1, so log2 f = 0 and 1 - f = 0).  Issued one chunk ahead
-// of gate_prep so the global-load latency is off the critical path.
+__device__ __forceinline__ float clamped_log2(float f) { return fmaxf(fast_log2(f), -64.f); }
+
+// Gates of chunk gc: lane l holds steps 2l, 2l+1 (t >= T reads as "no step":
+// f = 1, so log2 f = 0 and 1 - f = 0).  Loaded one chunk ahead of use.
 __device__ __forceinline__ float2 gate_load(const float* fh, int T, int gc, int lane) {
   const int t = gc * CH + 2 * lane;
   float2 r;
@@ -139,11 +170,17 @@ __device__ __forceinline__ float2 gate_load(const float* fh, int T, int gc, int 
   return r;
 }
 
-// One warp: gate arrays of one chunk from its gates (see gate_load).
-__device__ __forceinline__ void gate_prep(GateBuf* gb, float2 fv, int lane) {
-  const int tl = 2 * lane;
-  const float x0 = fmaxf(fast_log2(fv.x), -64.f), x1 = fmaxf(fast_log2(fv.y), -64.f);
-  const float w0 = 1.f - fv.x, w1 = 1.f - fv.y;
+// Chunk-local gate values, held by every warp for itself: lane l owns steps
+// 2l and 2l+1 (inclusive log2 cumulative gate l, 1 - f as w); tot is the log2
+// decay of the whole chunk (all lanes).
+struct WGates {
+  float l0, l1, w0, w1, tot;
+};
+__device__ __forceinline__ WGates warp_gates(float2 fv, int lane) {
+  WGates gt;
+  const float x0 = clamped_log2(fv.x), x1 = clamped_log2(fv.y);
+  gt.w0 = 1.f - fv.x;
+  gt.w1 = 1.f - fv.y;
   const float pair = x0 + x1;
   float inc = pair;
 #pragma unroll
@@ -151,64 +188,72 @@ __device__ __forceinline__ void gate_prep(GateBuf* gb, float2 fv, int lane) {
     const float y = __shfl_up_sync(0xffffffffu, inc, o);
     if (lane >= o) inc += y;
   }
-  const float l0 = inc - pair + x0, l1 = inc;
-  const float tot = __shfl_sync(0xffffffffu, inc, 31);
-  gb->lg[tl] = l0;
-  gb->lg[tl + 1] = l1;
-  gb->wv[tl] = w0;
-  gb->wv[tl + 1] = w1;
-  gb->ck[tl] = fast_exp2(tot - l0) * w0;
-  gb->ck[tl + 1] = fast_exp2(tot - l1) * w1;
-  gb->ea[tl] = fast_exp2(l0);
-  gb->ea[tl + 1] = fast_exp2(l1);
-  if (lane == 0) gb->lgC = tot;
+  gt.l0 = inc - pair + x0;
+  gt.l1 = inc;
+  gt.tot = __shfl_sync(0xffffffffu, inc, 31);
+  return gt;
 }
+// Value of step r (0..63) of a per-step quantity held as (v0, v1) pairs.
+__device__ __forceinline__ float step_val(float v0, float v1, int r) {
+  const float a = __shfl_sync(0xffffffffu, v0, r >> 1);
+  const float b = __shfl_sync(0xffffffffu, v1, r >> 1);
+  return (r & 1) ? b : a;
+}
+__device__ __forceinline__ bool factorises(const WGates& gt) { return gt.tot >= kFactorMin; }
 
-// acc (this warp's 16 state rows x 64 cols) += K~^T V for one chunk tile pair.
-__device__ __forceinline__ void add_ktv(float (&acc)[8][4], uint32_t kbase, uint32_t vbase,
-                                        const float* ck, int warp, int lane) {
-  const int mi = lane >> 3, r = lane & 7, c4 = lane & 3;
-  const int i0 = warp * 16;
+// Rows this thread scales when building a 64x64 tile: 4w + lane/8 and 32 + that.
+__device__ __forceinline__ int build_row(int tid, int j) { return (tid + NTHREADS * j) >> 3; }
+
+// dst rows (r, swizzled 128-byte rows) = scale_r * src rows, for this thread's
+// two rows (see build_row), 16 bytes each.
+__device__ __forceinline__ void build_rows(uint8_t* dst, const uint8_t* src, float s0, float s1,
+                                           int tid) {
 #pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    const int s0 = kk * 16;
-    uint32_t a[4];
-    ldsm_x4_t(a, kbase + sw128(s0 + (mi >> 1) * 8 + r, (i0 >> 3) + (mi & 1)));
-    const int sa = s0 + 2 * c4, sb = sa + 8;
-    const float ca0 = ck[sa], ca1 = ck[sa + 1], cb0 = ck[sb], cb1 = ck[sb + 1];
-    a[0] = scale_bf16x2(a[0], ca0, ca1);
-    a[1] = scale_bf16x2(a[1], ca0, ca1);
-    a[2] = scale_bf16x2(a[2], cb0, cb1);
-    a[3] = scale_bf16x2(a[3], cb0, cb1);
-#pragma unroll
-    for (int np = 0; np < 4; ++np) {
-      uint32_t b[4];
-      ldsm_x4_t(b, vbase + sw128(s0 + (mi & 1) * 8 + r, np * 2 + (mi >> 1)));
-      mma_bf16(acc[2 * np], a, b[0], b[1]);
-      mma_bf16(acc[2 * np + 1], a, b[2], b[3]);
-    }
+  for (int j = 0; j < 2; ++j) {
+    const int q = tid + NTHREADS * j, row = q >> 3, chunk = q & 7;
+    const uint32_t off = sw128(row, chunk);
+    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
+    const float c = j ? s1 : s0;
+    uint4 w;
+    w.x = scale_bf16x2(v.x, c, c);
+    w.y = scale_bf16x2(v.y, c, c);
+    w.z = scale_bf16x2(v.z, c, c);
+    w.w = scale_bf16x2(v.w, c, c);
+    *reinterpret_cast<uint4*>(dst + off) = w;
   }
 }
 
-// Write this thread's fragment of a 64x64 fp32 state as bf16 into a swizzled tile.
-__device__ __forceinline__ void store_state_bf16(uint8_t* tile, const float (&s)[8][4], int i_lo,
-                                                 int c4) {
+// Fragment geometry of a thread in the 8-warp layout: rows r0 and r0 + 8,
+// columns 8 * (4 hf + n) + 2 c4 (+1) for n = 0..3.
+struct Frag {
+  int r0, hf, c4;
+};
+
+__device__ __forceinline__ void store_frag_bf16(uint8_t* tile, const float (&s)[4][4], Frag fr) {
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const uint32_t col = 4u * c4;
-    *reinterpret_cast<uint32_t*>(tile + sw128(i_lo, n) + col) = pack_bf16(s[n][0], s[n][1]);
-    *reinterpret_cast<uint32_t*>(tile + sw128(i_lo + 8, n) + col) = pack_bf16(s[n][2], s[n][3]);
+  for (int n = 0; n < 4; ++n) {
+    const uint32_t chunk = 4 * fr.hf + n, col = 4u * fr.c4;
+    *reinterpret_cast<uint32_t*>(tile + sw128(fr.r0, chunk) + col) = pack_bf16(s[n][0], s[n][1]);
+    *reinterpret_cast<uint32_t*>(tile + sw128(fr.r0 + 8, chunk) + col) = pack_bf16(s[n][2], s[n][3]);
   }
 }
 
-// Write this thread's fragment of a 64x64 fp32 state row-major to global memory.
-__device__ __forceinline__ void store_state_rowmajor(float* dst, const float (&s)[8][4], int i_lo,
-                                                     int c4) {
+__device__ __forceinline__ void store_frag_rowmajor(float* dst, const float (&s)[4][4], Frag fr) {
 #pragma unroll
-  for (int n = 0; n < 8; ++n) {
-    const int j = n * 8 + 2 * c4;
-    *reinterpret_cast<float2*>(dst + i_lo * D + j) = make_float2(s[n][0], s[n][1]);
-    *reinterpret_cast<float2*>(dst + (i_lo + 8) * D + j) = make_float2(s[n][2], s[n][3]);
+  for (int n = 0; n < 4; ++n) {
+    const int j = 8 * (4 * fr.hf + n) + 2 * fr.c4;
+    *reinterpret_cast<float2*>(dst + fr.r0 * D + j) = make_float2(s[n][0], s[n][1]);
+    *reinterpret_cast<float2*>(dst + (fr.r0 + 8) * D + j) = make_float2(s[n][2], s[n][3]);
+  }
+}
+
+__device__ __forceinline__ void load_frag_rowmajor(float (&s)[4][4], const float* src, Frag fr) {
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const int j = 8 * (4 * fr.hf + n) + 2 * fr.c4;
+    const float2 lo = __ldg(reinterpret_cast<const float2*>(src + fr.r0 * D + j));
+    const float2 hi = __ldg(reinterpret_cast<const float2*>(src + (fr.r0 + 8) * D + j));
+    s[n][0] = lo.x; s[n][1] = lo.y; s[n][2] = hi.x; s[n][3] = hi.y;
   }
 }
 
@@ -220,21 +265,38 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int g = lane >> 2, c4 = lane & 3, mi = lane >> 3, r8 = lane & 7;
-  const int i_lo = warp * 16 + g;
-  GateBuf* gbuf = reinterpret_cast<GateBuf*>(smem + SM_GATE);
+  const int qd = warp & 3, hf = warp >> 2, g = lane >> 2, c4 = lane & 3;
+  const Frag fr{qd * 16 + g, hf, c4};
+  const int br0 = build_row(tid, 0), br1 = build_row(tid, 1);
+  float* lsuf = reinterpret_cast<float*>(smem + SM_LSUF);
   volatile uint32_t* bc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* bars1 = bars + STAGES;
+  uint64_t* bar_k = bars + STAGES + P1_STAGES;   // pass-1 MMA commits (2)
+  uint64_t* bar_m1 = bar_k + 2;                  // pass-2: P, Q^ S of a chunk
+  uint64_t* bar_m2 = bar_k + 3;                  // pass-2: P' V of a chunk
+  uint64_t* bar_m3 = bar_k + 4;                  // pass-2: K~^T V of a chunk
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM_TSLOT);
+  uint8_t* kt_tile = smem + SM_KT;
+  uint8_t* qt_tile = smem + SM_QT;
+  uint8_t* pt_tile = smem + SM_PT;
+  uint8_t* s_tile = smem + SM_SBUF;
 
+  if (warp == 0) tmem_alloc(tslot, TMEM_COLS);
   if (tid == 0) {
     uint32_t epoch;
     bc[0] = take_ticket(p.hdr, &epoch);
     bc[1] = epoch;
 #pragma unroll
-    for (int s = 0; s < STAGES + P1_STAGES; ++s) mbar_init(&bars[s], 1);
+    for (int s = 0; s < NBARS; ++s) mbar_init(&bars[s], 1);
     fence_barrier_init();
   }
+  tc_fence_before();
   __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  // this warp's accumulator slice: lanes 32 qd.., columns 32 hf..
+  const uint32_t tw = tbase + ((uint32_t)(32 * qd) << 16) + 32u * hf;
   const uint32_t unit = bc[0], epoch = bc[1];
   const int BH = p.BH, T = p.T;
   const int stripe = (int)unit / BH, bh = (int)unit % BH;
@@ -247,6 +309,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   const int n1 = need_p1 ? nc : 0;
   const int nit = n1 + (need_p2 ? nc : 0);
   const float* fh = p.f + (size_t)bh * T;
+  uint32_t ph_m1 = 0, ph_m2 = 0, ph_m3 = 0;
+  bool ok = true;
   MOGT_MARK(unit, 0);
 
   uint64_t pol_keep = 0, pol_stream = 0;
@@ -254,7 +318,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_keep));
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_stream));
   }
-  uint64_t* bars1 = bars + STAGES;
   // TMA loads of pipeline iteration `it` (thread 0 only).  Pass-1 iterations
   // use the 5-slot k/v ring, pass-2 iterations the 3-slot q/k/v ring.
   auto issue = [&](int it) {
@@ -275,62 +338,86 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       tma_load_3d_hint(base + 2 * TILE, &tv, &bars[slot], 0, t0, bh, pol_stream);
     }
   };
-  // pass-1 loads may run P1_STAGES - 1 ahead; pass-2 loads STAGES - 1 ahead
-  // and only once pass 1 has released the shared ring
-  auto issue_upto = [&](int it_done) {
-    // called at the top of iteration it_done (after the CTA barrier)
-    if (it_done < n1) {
-      const int nxt = it_done + P1_STAGES - 1;
-      if (nxt < n1) issue(nxt);
-    } else {
-      const int nxt = it_done + STAGES - 1;
-      if (nxt >= n1 + STAGES - 1) issue(nxt);
-    }
+  auto wait_bar = [&](uint64_t* bar, uint32_t ph) {
+    if (!mbar_wait(bar, ph)) ok = false;
   };
-  auto chunk_of = [&](int it) { return c_begin + (it < n1 ? it : it - n1); };
 
   if (tid == 0) {
     if (n1 > 0)
-      for (int it = 0; it < P1_STAGES - 1 && it < n1; ++it) issue(it);
+      for (int it = 0; it < P1_AHEAD && it < n1; ++it) issue(it);
     else
       for (int it = 0; it < STAGES - 1; ++it) issue(it);
   }
-  // warp 0 prepares the gate arrays one chunk ahead; fpre holds the gates of
-  // the next iteration, loaded one iteration before they are needed
-  float2 fpre = make_float2(1.f, 1.f);
-  if (warp == 0 && nit > 0) {
-    gate_prep(&gbuf[0], gate_load(fh, T, chunk_of(0), lane), lane);
-    if (nit > 1) fpre = gate_load(fh, T, chunk_of(1), lane);
-  }
-  auto gates_next = [&](int it) {
-    if (warp == 0 && it + 1 < nit) {
-      gate_prep(&gbuf[(it + 1) & 1], fpre, lane);
-      if (it + 2 < nit) fpre = gate_load(fh, T, chunk_of(it + 2), lane);
-    }
-  };
 
-  // ---------------- pass 1: stripe aggregate ----------------
-  float agg[8][4];
+  // ---------------- pass 1: stripe aggregate in tensor memory ----------------
+  float agg[4][4];
 #pragma unroll
-  for (int n = 0; n < 8; ++n)
+  for (int n = 0; n < 4; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) agg[n][e] = 0.f;
   float ltot = 0.f;
-  for (int it = 0; it < n1; ++it) {
+  if (n1 > 0) {
+    // suffix log2 decays: lsuf[c] = sum of the chunk log2 decays after c
+    for (int c = warp; c < n1; c += NTHREADS / 32) {
+      const float2 fv = gate_load(fh, T, c_begin + c, lane);
+      float x = clamped_log2(fv.x) + clamped_log2(fv.y);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) lsuf[c] = x;
+    }
     __syncthreads();
-    if (tid == 0) issue_upto(it);
-    gates_next(it);
-    if (!mbar_wait(&bars1[it % P1_STAGES], (it / P1_STAGES) & 1)) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
-    const GateBuf* gb = &gbuf[it & 1];
-    const uint8_t* base = smem + SM_RING + (it % P1_STAGES) * 2 * TILE - TILE;
-    const float lgC = gb->lgC;
-    const float dC = fast_exp2(lgC);
-    ltot += lgC;
+    if (warp == 0) {
+      const int per = (n1 + 31) / 32, c0 = lane * per, c1 = min(c0 + per, n1);
+      float part = 0.f;
+      for (int c = c0; c < c1; ++c) part += lsuf[c];
+      float sfx = part;  // inclusive suffix over lanes >= lane
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) agg[n][e] *= dC;
-    add_ktv(agg, smem_u32(base + TILE), smem_u32(base + 2 * TILE), gb->ck, warp, lane);
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_down_sync(0xffffffffu, sfx, o);
+        if (lane + o < 32) sfx += y;
+      }
+      if (lane == 0) bc[2] = __float_as_uint(sfx);
+      float run = sfx - part;  // sum over the chunks after this lane's block
+      for (int c = c1 - 1; c >= c0; --c) {
+        const float x = lsuf[c];
+        lsuf[c] = run;
+        run += x;
+      }
+    }
+    __syncthreads();
+  }
+  {
+    float2 fnext = n1 > 0 ? gate_load(fh, T, c_begin, lane) : make_float2(1.f, 1.f);
+    for (int c = 0; c < n1; ++c) {
+      const WGates gt = warp_gates(fnext, lane);
+      if (c + 1 < n1) fnext = gate_load(fh, T, c_begin + c + 1, lane);
+      if (c >= 2) wait_bar(&bar_k[c & 1], ((c - 2) >> 1) & 1);  // MMA of chunk c-2 done
+      if (tid == 0 && c + P1_AHEAD < n1) issue(c + P1_AHEAD);    // into chunk c-2's slot
+      if (!mbar_wait(&bars1[c % P1_STAGES], (c / P1_STAGES) & 1)) ok = false;
+      // K~ rows: decay(s -> stripe end) (1 - f_s) = exp2(lsuf + tot - l_s) (1 - f_s)
+      const float sc = lsuf[c] + gt.tot;
+      const float k0 = fast_exp2(sc - gt.l0) * gt.w0, k1 = fast_exp2(sc - gt.l1) * gt.w1;
+      const float s0 = step_val(k0, k1, br0), s1 = step_val(k0, k1, br1);
+      uint8_t* base = smem + SM_RING + (c % P1_STAGES) * 2 * TILE;
+      uint8_t* kt = (c & 1) ? qt_tile : kt_tile;
+      build_rows(kt, base, s0, s1, tid);
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_DS, smem_u32(kt), true, smem_u32(base + TILE), true, c > 0);
+        umma_commit(&bar_k[c & 1]);
+      }
+      __syncwarp();
+    }
+  }
+  if (n1 > 0) {
+    wait_bar(&bar_k[(n1 - 1) & 1], ((n1 - 1) >> 1) & 1);  // all pass-1 MMAs done
+    tc_fence_after();
+    tmem_ld_16x32(agg, tw + TM_DS);
+    tc_fence_before();
+    ltot = __uint_as_float(bc[2]);
   }
   MOGT_MARK(unit, 1);
   if (n1 > 0) {
@@ -341,12 +428,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       for (int it = n1; it < n1 + STAGES - 1; ++it) issue(it);
   }
   const float A_agg = fast_exp2(ltot);
-  const size_t st_off = (size_t)unit * (D * D) + (size_t)tid * 32;
+  const size_t st_off = (size_t)unit * (D * D) + (size_t)tid * 16;
 
   if (n1 > 0 && stripe > 0 && has_succ) {
     float4* dst = reinterpret_cast<float4*>(p.st_agg + st_off);
 #pragma unroll
-    for (int n = 0; n < 8; ++n) __stcg(dst + n, make_float4(agg[n][0], agg[n][1], agg[n][2], agg[n][3]));
+    for (int n = 0; n < 4; ++n) __stcg(dst + n, make_float4(agg[n][0], agg[n][1], agg[n][2], agg[n][3]));
     if (tid == 0) __stcg(p.a_agg + unit, A_agg);
     __threadfence();
     __syncthreads();
@@ -354,181 +441,249 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   }
 
   // ---------------- state entering the stripe ----------------
-  float sin[8][4];
+  float sin[4][4];
   float a_in = 1.f;
   if (stripe == 0) {
+    if (p.S0) {
+      load_frag_rowmajor(sin, p.S0 + (size_t)bh * D * D, fr);
+    } else {
 #pragma unroll
-    for (int n = 0; n < 8; ++n) {
-      const int j = n * 8 + 2 * c4;
-      if (p.S0) {
-        const float* s0p = p.S0 + (size_t)bh * D * D;
-        const float2 lo = __ldg(reinterpret_cast<const float2*>(s0p + i_lo * D + j));
-        const float2 hi = __ldg(reinterpret_cast<const float2*>(s0p + (i_lo + 8) * D + j));
-        sin[n][0] = lo.x; sin[n][1] = lo.y; sin[n][2] = hi.x; sin[n][3] = hi.y;
-      } else {
-        sin[n][0] = sin[n][1] = sin[n][2] = sin[n][3] = 0.f;
-      }
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sin[n][e] = 0.f;
     }
   } else {
     LookbackBufs lb{p.flags, p.a_agg, p.a_inc, p.st_agg, p.st_inc, p.hdr};
-    lookback_scalar_state(sin, a_in, lb, stripe, (uint32_t)bh, (uint32_t)BH, epoch, unit,
-                          reinterpret_cast<float*>(smem + SM_MISC + 64),
-                          reinterpret_cast<volatile uint32_t*>(smem + SM_MISC + 16));
+    lookback_scalar_state<4>(sin, a_in, lb, stripe, (uint32_t)bh, (uint32_t)BH, epoch, unit,
+                             reinterpret_cast<float*>(smem + SM_MISC + 64),
+                             reinterpret_cast<volatile uint32_t*>(smem + SM_MISC + 16));
   }
   MOGT_MARK(unit, 2);
 
   if (n1 > 0) {
-    float inc_st[8][4];
+    float inc_st[4][4];
 #pragma unroll
-    for (int n = 0; n < 8; ++n)
+    for (int n = 0; n < 4; ++n)
 #pragma unroll
-      for (int e = 0; e < 4; ++e) inc_st[n][e] = A_agg * sin[n][e] + agg[n][e];
+      for (int e = 0; e < 4; ++e) inc_st[n][e] = fmaf(A_agg, sin[n][e], agg[n][e]);
     if (has_succ) {
       float4* dst = reinterpret_cast<float4*>(p.st_inc + st_off);
 #pragma unroll
-      for (int n = 0; n < 8; ++n)
+      for (int n = 0; n < 4; ++n)
         __stcg(dst + n, make_float4(inc_st[n][0], inc_st[n][1], inc_st[n][2], inc_st[n][3]));
       if (tid == 0) __stcg(p.a_inc + unit, A_agg * a_in);
       __threadfence();
       __syncthreads();
       if (tid == 0) st_release_u32(p.flags + unit, flag_tag(epoch, kFlagInc));
     } else {
-      if (p.S_final) store_state_rowmajor(p.S_final + (size_t)bh * D * D, inc_st, i_lo, c4);
+      if (p.S_final) store_frag_rowmajor(p.S_final + (size_t)bh * D * D, inc_st, fr);
       if (tid == 0 && p.decay_final) p.decay_final[bh] = A_agg * a_in;
     }
   }
   MOGT_MARK(unit, 3);
 
   // ---------------- pass 2: outputs ----------------
+  // Software pipeline, one CTA barrier per chunk.  In iteration c:
+  //   wait the MMAs of chunk c (P, K~^T V, O_c = Q^ S_c, issued an iteration
+  //   earlier) -> state S_{c+1} -> write the output of chunk c-1 -> mask P_c ->
+  //   build Q^, K~ of chunk c+1 -> barrier -> one thread issues O_c += P'_c V_c
+  //   and the state-independent MMAs of chunk c+1 and the TMA of chunk c+2.
+  // O is double-buffered in tensor memory; the other operands are single.
   if (need_p2) {
-    store_state_bf16(smem + SM_SBUF + (n1 & 1) * TILE, sin, i_lo, c4);
     const bool final_here = !has_succ && n1 == 0;
+    const int gc0 = c_begin;
+    float2 fnext = gate_load(fh, T, gc0, lane);
+    WGates gcur = warp_gates(fnext, lane);
+    if (nc > 1) fnext = gate_load(fh, T, gc0 + 1, lane);
     float ltot2 = 0.f;
-    for (int it = n1; it < nit; ++it) {
-      const int c = it - n1, gc = c_begin + c;
-      __syncthreads();
-      if (tid == 0) issue_upto(it);
-      gates_next(it);
-      if (p.seg_states && (gc % SEG_CHUNKS) == 0)
-        store_state_rowmajor(p.seg_states + ((size_t)bh * p.nseg + gc / SEG_CHUNKS) * D * D, sin,
-                             i_lo, c4);
-      if (!mbar_wait(&bars[c % STAGES], (c / STAGES) & 1)) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
-      const GateBuf* gb = &gbuf[it & 1];
-      uint8_t* base = smem + SM_RING + (c % STAGES) * SLOT;
+    // build the chunk-0 operands and issue its MMAs
+    auto build_chunk = [&](int c, const WGates& gt) {
+      // Q^ = diag(exp2 l_t) Q, K~ = diag(w_s exp2(-l_s)) K (factorised) or
+      // diag(w_s exp2(lgC - l_s)) K (exact)
+      const uint8_t* base = smem + SM_RING + (c % STAGES) * SLOT;
+      const bool fast = factorises(gt);
+      const float e0 = fast_exp2(gt.l0), e1 = fast_exp2(gt.l1);
+      const float k0 = gt.w0 > 0.f ? gt.w0 * fast_exp2((fast ? 0.f : gt.tot) - gt.l0) : 0.f;
+      const float k1 = gt.w1 > 0.f ? gt.w1 * fast_exp2((fast ? 0.f : gt.tot) - gt.l1) : 0.f;
+      build_rows(kt_tile, base + TILE, step_val(k0, k1, br0), step_val(k0, k1, br1), tid);
+      if (want_out) build_rows(qt_tile, base, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+    };
+    // The MMA groups of a chunk touch disjoint tensor memory and are issued
+    // by lane 0 of different warps so their issue latencies overlap:
+    //   warp 1: P = Q^ K~^T (factorised) or Q K^T, and O_c = Q^ S_c -> bar_m1
+    //   warp 2: dS = K~^T V                                       -> bar_m3
+    //   warp 0: O_c += P' V (after the mask)                      -> bar_m2
+    //   warp 3: TMA of the chunk two ahead
+    auto issue_mma1 = [&](int c, bool fast) {
+      const uint8_t* base = smem + SM_RING + (c % STAGES) * SLOT;
       const uint32_t qb = smem_u32(base), kb = smem_u32(base + TILE), vb = smem_u32(base + 2 * TILE);
-      const uint32_t sb = smem_u32(smem + SM_SBUF + (it & 1) * TILE);
-      if (want_out) {
-        const int rq = warp * 16;
-        uint32_t qa[4][4];
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) ldsm_x4(qa[kk], qb + sw128(rq + (lane & 15), kk * 2 + (lane >> 4)));
-        float oacc[8][4];
-#pragma unroll
-        for (int n = 0; n < 8; ++n)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) oacc[n][e] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            uint32_t b[4];
-            ldsm_x4_t(b, sb + sw128(kk * 16 + (mi & 1) * 8 + r8, np * 2 + (mi >> 1)));
-            mma_bf16(oacc[2 * np], qa[kk], b[0], b[1]);
-            mma_bf16(oacc[2 * np + 1], qa[kk], b[2], b[3]);
-          }
-        {
-          const float e0 = gb->ea[rq + g], e1 = gb->ea[rq + g + 8];
-#pragma unroll
-          for (int n = 0; n < 8; ++n) {
-            oacc[n][0] *= e0; oacc[n][1] *= e0;
-            oacc[n][2] *= e1; oacc[n][3] *= e1;
-          }
+      if (warp == 1 && lane == 0) {
+        tc_fence_after();
+        if (want_out) {
+          if (fast)
+            umma_64x64x64(tbase + TM_P, smem_u32(qt_tile), false, smem_u32(kt_tile), false, false);
+          else
+            umma_64x64x64(tbase + TM_P, qb, false, kb, false, false);
+          umma_64x64x64(tbase + TM_O0 + 64u * (c & 1), smem_u32(qt_tile), false, smem_u32(s_tile),
+                        true, false);
         }
-        float pacc[8][4];
+        umma_commit(bar_m1);
+      } else if (warp == 2 && lane == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_DS, smem_u32(kt_tile), true, vb, true, false);
+        umma_commit(bar_m3);
+      }
+    };
+    auto write_out = [&](int c) {
+      // output rows of chunk c from the O buffer of chunk c
+      float oacc[4][4];
+      tmem_ld_16x32(oacc, tw + TM_O0 + 64u * (c & 1));
+      const int ta = (gc0 + c) * CH + fr.r0, tb = ta + 8;
+      const size_t rowa = ((size_t)bh * T + ta) * D, rowb = ((size_t)bh * T + tb) * D;
 #pragma unroll
-        for (int n = 0; n < 8; ++n)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) pacc[n][e] = 0.f;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-#pragma unroll
-          for (int np = 0; np < 4; ++np) {
-            if (np <= warp) {
-              uint32_t b[4];
-              ldsm_x4(b, kb + sw128(np * 16 + (mi >> 1) * 8 + r8, kk * 2 + (mi & 1)));
-              mma_bf16(pacc[2 * np], qa[kk], b[0], b[1]);
-              mma_bf16(pacc[2 * np + 1], qa[kk], b[2], b[3]);
-            }
-          }
-        {
-          const int tl0 = rq + g, tl1 = tl0 + 8;
-          const float lt0 = gb->lg[tl0], lt1 = gb->lg[tl1];
-#pragma unroll
-          for (int n = 0; n < 8; ++n) {
-            if ((n >> 1) <= warp) {
-#pragma unroll
-              for (int e = 0; e < 2; ++e) {
-                const int s = n * 8 + 2 * c4 + e;
-                const float ls = gb->lg[s], ws = gb->wv[s];
-                pacc[n][e] = (s <= tl0) ? pacc[n][e] * fast_exp2(lt0 - ls) * ws : 0.f;
-                pacc[n][2 + e] = (s <= tl1) ? pacc[n][2 + e] * fast_exp2(lt1 - ls) * ws : 0.f;
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          if (kk <= warp) {
-            uint32_t a[4];
-            a[0] = pack_bf16(pacc[2 * kk][0], pacc[2 * kk][1]);
-            a[1] = pack_bf16(pacc[2 * kk][2], pacc[2 * kk][3]);
-            a[2] = pack_bf16(pacc[2 * kk + 1][0], pacc[2 * kk + 1][1]);
-            a[3] = pack_bf16(pacc[2 * kk + 1][2], pacc[2 * kk + 1][3]);
-#pragma unroll
-            for (int np = 0; np < 4; ++np) {
-              uint32_t b[4];
-              ldsm_x4_t(b, vb + sw128(kk * 16 + (mi & 1) * 8 + r8, np * 2 + (mi >> 1)));
-              mma_bf16(oacc[2 * np], a, b[0], b[1]);
-              mma_bf16(oacc[2 * np + 1], a, b[2], b[3]);
-            }
-          }
-        }
-        const int ta = gc * CH + rq + g, tb = ta + 8;
-        const size_t rowa = ((size_t)bh * T + ta) * D, rowb = ((size_t)bh * T + tb) * D;
-#pragma unroll
-        for (int n = 0; n < 8; ++n) {
-          const int j = n * 8 + 2 * c4;
-          if (OUT_F32) {
-            float* o = static_cast<float*>(p.o);
-            if (ta < T) __stcs(reinterpret_cast<float2*>(o + rowa + j), make_float2(oacc[n][0], oacc[n][1]));
-            if (tb < T) __stcs(reinterpret_cast<float2*>(o + rowb + j), make_float2(oacc[n][2], oacc[n][3]));
-          } else {
-            uint32_t* o = static_cast<uint32_t*>(p.o);
-            if (ta < T) __stcs(o + (rowa + j) / 2, pack_bf16(oacc[n][0], oacc[n][1]));
-            if (tb < T) __stcs(o + (rowb + j) / 2, pack_bf16(oacc[n][2], oacc[n][3]));
-          }
+      for (int n = 0; n < 4; ++n) {
+        const int j = 8 * (4 * hf + n) + 2 * c4;
+        if (OUT_F32) {
+          float* o = static_cast<float*>(p.o);
+          if (ta < T) __stcs(reinterpret_cast<float2*>(o + rowa + j), make_float2(oacc[n][0], oacc[n][1]));
+          if (tb < T) __stcs(reinterpret_cast<float2*>(o + rowb + j), make_float2(oacc[n][2], oacc[n][3]));
+        } else {
+          uint32_t* o = static_cast<uint32_t*>(p.o);
+          if (ta < T) __stcs(o + (rowa + j) / 2, pack_bf16(oacc[n][0], oacc[n][1]));
+          if (tb < T) __stcs(o + (rowb + j) / 2, pack_bf16(oacc[n][2], oacc[n][3]));
         }
       }
-      // running state for the next chunk (or the final state)
-      const float lgC = gb->lgC;
-      ltot2 += lgC;
+    };
+
+    if (p.seg_states && (gc0 % SEG_CHUNKS) == 0)
+      store_frag_rowmajor(p.seg_states + ((size_t)bh * p.nseg + gc0 / SEG_CHUNKS) * D * D, sin, fr);
+    store_frag_bf16(s_tile, sin, fr);
+    if (!mbar_wait(&bars[0], 0)) ok = false;
+    build_chunk(0, gcur);
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    issue_mma1(0, factorises(gcur));
+    __syncwarp();
+
+    for (int c = 0; c < nc; ++c) {
+      const int it = n1 + c;
+      const bool fast = factorises(gcur);
+      MOGT_CLK(unit, 5, c == 5);
+      wait_bar(bar_m1, ph_m1);
+      ph_m1 ^= 1u;
+      wait_bar(bar_m3, ph_m3);
+      ph_m3 ^= 1u;
+      tc_fence_after();
+      MOGT_CLK(unit, 6, c == 5);
+      // state for chunk c+1 (or the final state)
+      const float dC = fast_exp2(gcur.tot);
+      ltot2 += gcur.tot;
       if (c + 1 < nc || (final_here && p.S_final)) {
-        const float dC = fast_exp2(lgC);
+        float ds[4][4];
+        tmem_ld_16x32(ds, tw + TM_DS);
+        if (fast) {
 #pragma unroll
-        for (int n = 0; n < 8; ++n)
+          for (int n = 0; n < 4; ++n)
 #pragma unroll
-          for (int e = 0; e < 4; ++e) sin[n][e] *= dC;
-        add_ktv(sin, kb, vb, gb->ck, warp, lane);
-        if (c + 1 < nc) store_state_bf16(smem + SM_SBUF + ((it + 1) & 1) * TILE, sin, i_lo, c4);
+            for (int e = 0; e < 4; ++e) sin[n][e] = dC * (sin[n][e] + ds[n][e]);
+        } else {
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) sin[n][e] = fmaf(sin[n][e], dC, ds[n][e]);
+        }
+        if (c + 1 < nc) {
+          store_frag_bf16(s_tile, sin, fr);
+          const int gn = gc0 + c + 1;
+          if (p.seg_states && (gn % SEG_CHUNKS) == 0)
+            store_frag_rowmajor(p.seg_states + ((size_t)bh * p.nseg + gn / SEG_CHUNKS) * D * D, sin, fr);
+        }
       }
+      // output of the previous chunk
+      if (c > 0) {
+        wait_bar(bar_m2, ph_m2);
+        ph_m2 ^= 1u;
+        tc_fence_after();
+        if (want_out) write_out(c - 1);
+      }
+      MOGT_CLK(unit, 7, c == 5);
+      // P'_c: causal mask (and the exact decays when they do not factorise)
+      if (want_out) {
+        float pacc[4][4];
+        tmem_ld_16x32(pacc, tw + TM_P);
+        const int tl0 = fr.r0, tl1 = tl0 + 8;
+        if (fast) {
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int s = 8 * (4 * hf + n) + 2 * c4 + e;
+              if (s > tl0) pacc[n][e] = 0.f;
+              if (s > tl1) pacc[n][2 + e] = 0.f;
+            }
+        } else {
+          const float lt0 = step_val(gcur.l0, gcur.l1, tl0), lt1 = step_val(gcur.l0, gcur.l1, tl1);
+#pragma unroll
+          for (int n = 0; n < 4; ++n)
+#pragma unroll
+            for (int e = 0; e < 2; ++e) {
+              const int s = 8 * (4 * hf + n) + 2 * c4 + e;
+              const float ls = step_val(gcur.l0, gcur.l1, s), ws = step_val(gcur.w0, gcur.w1, s);
+              pacc[n][e] = (s <= tl0) ? pacc[n][e] * fast_exp2(lt0 - ls) * ws : 0.f;
+              pacc[n][2 + e] = (s <= tl1) ? pacc[n][2 + e] * fast_exp2(lt1 - ls) * ws : 0.f;
+            }
+        }
+        store_frag_bf16(pt_tile, pacc, fr);
+      }
+      MOGT_CLK(unit, 8, c == 5);
+      // operands of chunk c+1
+      WGates gnext = gcur;
+      if (c + 1 < nc) {
+        gnext = warp_gates(fnext, lane);
+        if (c + 2 < nc) fnext = gate_load(fh, T, gc0 + c + 2, lane);
+        if (!mbar_wait(&bars[(c + 1) % STAGES], ((c + 1) / STAGES) & 1)) ok = false;
+        build_chunk(c + 1, gnext);
+      }
+      MOGT_CLK(unit, 9, c == 5);
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();
+      MOGT_CLK(unit, 10, c == 5);
+      if (tid == 0) {
+        tc_fence_after();
+        if (want_out) {
+          const uint32_t vb = smem_u32(smem + SM_RING + (c % STAGES) * SLOT + 2 * TILE);
+          umma_64x64x64(tbase + TM_O0 + 64u * (c & 1), smem_u32(pt_tile), false, vb, true, true);
+        }
+        umma_commit(bar_m2);
+        MOGT_CLK(unit, 12, c == 5);
+      }
+      if (c + 1 < nc) issue_mma1(c + 1, factorises(gnext));
+      if (warp == 3 && lane == 0) issue(it + STAGES - 1);  // chunk c+2 into chunk c-1's slot
+      __syncwarp();
+      MOGT_CLK(unit, 13, c == 5);
+      gcur = gnext;
+      MOGT_CLK(unit, 11, c == 5);
     }
+    // output of the last chunk
+    wait_bar(bar_m2, ph_m2);
+    ph_m2 ^= 1u;
+    tc_fence_after();
+    if (want_out) write_out(nc - 1);
     if (final_here) {
-      if (p.S_final) store_state_rowmajor(p.S_final + (size_t)bh * D * D, sin, i_lo, c4);
+      if (p.S_final) store_frag_rowmajor(p.S_final + (size_t)bh * D * D, sin, fr);
       if (tid == 0 && p.decay_final) p.decay_final[bh] = a_in * fast_exp2(ltot2);
     }
   }
   MOGT_MARK(unit, 4);
+  if (!ok) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
+  tc_fence_before();
   __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
   if (tid == 0) finish_cta(p.hdr, epoch, gridDim.x);
 }
 

@@ -8,7 +8,8 @@
 // flags of up to 32 predecessors at once, finds the nearest inclusive one,
 // and all threads then accumulate the aggregates in between with pipelined
 // L2 loads.  States use the producer's fragment-native layout: thread `tid`
-// owns floats [tid*32, tid*32+32) of every 4096-float state.
+// owns floats [tid*4*NF, (tid+1)*4*NF) of every 4096-float state, so
+// NF * 4 * blockDim.x == 4096.
 #pragma once
 
 #include "common.cuh"
@@ -25,15 +26,16 @@ struct LookbackBufs {
 };
 
 // scl: 32 floats of shared memory; ctl: 4 words of shared memory.
-// Must be called by all 128 threads of the CTA.
-__device__ __forceinline__ void lookback_scalar_state(float (&acc)[8][4], float& a_in,
+// Must be called by all threads of the CTA.
+template <int NF>
+__device__ __forceinline__ void lookback_scalar_state(float (&acc)[NF][4], float& a_in,
                                                       const LookbackBufs& lb, int s_self,
                                                       uint32_t base, uint32_t stride,
                                                       uint32_t epoch, uint32_t unit_id, float* scl,
                                                       volatile uint32_t* ctl) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 #pragma unroll
-  for (int n = 0; n < 8; ++n)
+  for (int n = 0; n < NF; ++n)
 #pragma unroll
     for (int e = 0; e < 4; ++e) acc[n][e] = 0.f;
   const uint32_t want = epoch & 0x3FFFFFFFu;
@@ -101,10 +103,10 @@ __device__ __forceinline__ void lookback_scalar_state(float (&acc)[8][4], float&
       const uint32_t m = base + (uint32_t)(sp - l) * stride;
       const bool inc = end && l == n - 1;
       const float4* src = reinterpret_cast<const float4*>((inc ? lb.st_inc : lb.st_agg) +
-                                                          (size_t)m * 4096 + (size_t)tid * 32);
+                                                          (size_t)m * 4096 + (size_t)tid * (4 * NF));
       const float s = scl[l];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q = 0; q < NF; ++q) {
         const float4 v = __ldcg(src + q);
         acc[q][0] = fmaf(s, v.x, acc[q][0]);
         acc[q][1] = fmaf(s, v.y, acc[q][1]);

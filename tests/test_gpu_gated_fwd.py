@@ -89,7 +89,8 @@ def test_segment_states_and_state_only_mode(mg):
     # state-only (first phase of the sequence-parallel scan): no q, no o
     _, S2, dec2, _ = m.ops.gated_scan_fwd(None, k.cuda(), v.cuda(), f.cuda(), want_final=True,
                                           want_output=False)
-    assert torch.allclose(S2, S_fin, rtol=1e-5, atol=1e-6)
+    # pass-1 (state-only) and pass-2 state paths round bf16 operands differently
+    assert float((S2 - S_fin).abs().max() / S_fin.abs().max()) <= TOL_BF16
     assert torch.allclose(dec2, dec)
 
 
