@@ -107,6 +107,24 @@ int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v, con
                                 int in_dtype, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Headed gated scan, backward: gradients of L = sum_t <o_t, do_t>.
+ * Replaces the reference's backward for this operator, affine_scan.py:65-124
+ * (affine_scan_sequential_backward: Sigma_t = g_t + U_{t+1}^T Sigma_{t+1},
+ * dU_t = Sigma_t H_{t-1}^T), chained through U = f I, V = (1-f) k v^T and the
+ * readout (g_t = q_t do_t^T).
+ *   inputs as mogt_gated_scan_fwd, d_o : [BH, T, dv] (same dtype as q)
+ *   dq, dk : [BH, T, dk], dv : [BH, T, dv] in the input dtype; df : [BH, T] fp32
+ *   dS0 : [BH, dk, dv] fp32 gradient of the initial state S0, or NULL
+ *   in_dtype MOGT_DTYPE_F32: exact sequential kernels (dk, dv <= 128).
+ * ------------------------------------------------------------------------- */
+size_t mogt_gated_scan_bwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                                           int in_dtype);
+int mogt_gated_scan_bwd(const void* q, const void* k, const void* v, const float* f,
+                        const void* d_o, const float* S0, void* dq, void* dk, void* dv, float* df,
+                        float* dS0, int64_t BH, int64_t T, int64_t dk_, int64_t dv_, int in_dtype,
+                        void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).
  * Replaces triton_scan.py:232-311 (_triton_affine_scan_hybrid_forward: local
  * Triton kernel + Python carry scan + carry apply), triton_scan.py:151-175

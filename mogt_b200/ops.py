@@ -11,7 +11,7 @@ import torch
 
 from . import _native as N
 
-__all__ = ["gated_scan_fwd", "affine_scan", "affine_grad_u", "gated_num_segments"]
+__all__ = ["gated_scan_fwd", "gated_scan_bwd", "affine_scan", "affine_grad_u", "gated_num_segments"]
 
 
 def _require_cuda(*ts, what):
@@ -75,6 +75,38 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
                                    N.ptr(ws), ws.numel(), N.stream_ptr(dev))
     N.check(st, "mogt_gated_scan_fwd")
     return o, S_fin, dec, seg
+
+
+def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False):
+    """Gradients of sum(o * do) for o = gated_scan(q, k, v, f): returns
+    (dq, dk, dv, df, dS0) with dq, dk, dv in the input dtype, df fp32 and dS0
+    (gradient of the initial state) fp32 or None."""
+    _require_cuda(q, k, v, f, do, initial_state, what="gated_scan backward")
+    B, H, T, dk = k.shape
+    dv = v.shape[-1]
+    if q.shape != k.shape or v.shape[:3] != (B, H, T) or f.shape != (B, H, T) or do.shape != v.shape:
+        raise ValueError("q, k: [B, H, T, dk]; v, do: [B, H, T, dv]; f: [B, H, T]")
+    dt = k.dtype
+    if dt != torch.float32:
+        raise ValueError("the gated-scan backward currently takes float32 inputs")
+    dev = k.device
+    q, k, v, do = (t.to(dt).contiguous() for t in (q, k, v, do))
+    f = f.to(torch.float32).contiguous()
+    S0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    gq, gk = torch.empty_like(q), torch.empty_like(k)
+    gv = torch.empty_like(v)
+    gf = torch.empty(B, H, T, dtype=torch.float32, device=dev)
+    gS0 = torch.empty(B, H, dk, dv, dtype=torch.float32, device=dev) if want_dS0 else None
+    L = N.lib()
+    code = N.dtype_code(dt)
+    nbytes = L.mogt_gated_scan_bwd_workspace_bytes(B * H, T, dk, dv, code)
+    with torch.cuda.device(dev):
+        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        st = L.mogt_gated_scan_bwd(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(do), N.ptr(S0),
+                                   N.ptr(gq), N.ptr(gk), N.ptr(gv), N.ptr(gf), N.ptr(gS0), B * H, T,
+                                   dk, dv, code, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
+    N.check(st, "mogt_gated_scan_bwd")
+    return gq, gk, gv, gf, gS0
 
 
 def _check_uv(U, V):
