@@ -333,8 +333,11 @@ def run_b200(args):
     ok = torch.equal(ho.to(dev), o_dev[0])
 
     extra = {}
-    if not args.no_extra and rank == 0:
-        extra = extra_affine(dev)
+    if not args.no_extra:
+        bb = extra_backbone(dev, world, rank)
+        if rank == 0:
+            extra = extra_affine(dev)
+            extra["backbone"] = bb
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -400,6 +403,50 @@ def extra_affine(dev):
     return {"affine_r16_c48_L32768": {"ms": ms, "GBps": alg / (ms / 1e3) / 1e9,
                                       "reference_L4_triton_hybrid_ms": 5.48,
                                       "note": "not L2-flushed (235 MB working set > L2)"}}
+
+
+def extra_backbone(dev, world, rank):
+    """MOGT backbone forward (d768, 4 layers, r=16, vocab
+    32000, identity connection + rank-wise coupled gate), T=32768, bf16
+    autocast, global batch 8 split over the ranks, random N(0, 0.02) weights;
+    whole-job tokens/s with the time taken as the max over ranks."""
+    import torch
+    import torch.distributed as dist
+    from mogt_b200.backbone import MOGTModel, configure_identity_coupled
+    T, layers, global_b = 32768, 4, 8
+    b_local = max(1, global_b // world)
+    torch.manual_seed(1234 + rank)
+    model = MOGTModel(32000, 768, layers, 16)
+    for p in model.parameters():
+        torch.nn.init.normal_(p, std=0.02)
+    configure_identity_coupled(model)
+    model = model.to(dev).eval()
+    ids = torch.randint(0, 32000, (b_local, T), device=dev)
+    def run():
+        with torch.inference_mode(), torch.autocast("cuda", dtype=torch.bfloat16):
+            return model(ids)
+    for _ in range(2):
+        run()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 3
+    e0.record()
+    for _ in range(n):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    del model
+    torch.cuda.empty_cache()
+    return {"tokens_per_s": b_local * world * T / (ms / 1e3), "ms_per_step": ms,
+            "config": f"d768 r16 4 layers vocab 32000, B={b_local}/GPU x {world}, T={T}, bf16 autocast",
+            "reference_L4_2layer_B1_tokens_per_s": 422000}
 
 
 def main():
