@@ -338,6 +338,7 @@ def run_b200(args):
         if rank == 0:
             extra = extra_affine(dev)
             extra["backbone"] = bb
+            extra["matrix_scan_config3"] = extra_matrix(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -403,6 +404,40 @@ def extra_affine(dev):
     return {"affine_r16_c48_L32768": {"ms": ms, "GBps": alg / (ms / 1e3) / 1e9,
                                       "reference_L4_triton_hybrid_ms": 5.48,
                                       "note": "not L2-flushed (235 MB working set > L2)"}}
+
+
+def extra_matrix(dev):
+    """dense Cayley transitions, B=2, H=8, T=8192, d=64,
+    bf16 q/k/v, fp32 A; minimal flops per (step, head) 2*64^3 + 2*64^2 + 2*64^2
+    = 540,672 and bytes 16,900 (A 16384 + q,k,v 384 + f 4 + o 128)."""
+    import torch
+    from mogt_b200 import ops
+    B, H, T, d = 2, 8, 8192, 64
+    g = torch.Generator(device=dev).manual_seed(11)
+    M = torch.randn(B, H, T, d, d, generator=g, device=dev)
+    W = 0.05 * (M - M.transpose(-1, -2))
+    I = torch.eye(d, device=dev)
+    A = torch.linalg.solve(I - W, I + W)
+    del M, W
+    q, k, v = (torch.randn(B, H, T, d, generator=g, device=dev).bfloat16() for _ in range(3))
+    f = torch.sigmoid(torch.randn(B, H, T, generator=g, device=dev) + 2.0)
+    for _ in range(2):
+        ops.matrix_scan_fwd(A, q, k, v, f)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 3
+    e0.record()
+    for _ in range(n):
+        ops.matrix_scan_fwd(A, q, k, v, f)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    units = B * H * T
+    del A
+    torch.cuda.empty_cache()
+    return {"ms": ms, "TFLOPs": units * 540672 / (ms / 1e3) / 1e12,
+            "GBps": units * 16900 / (ms / 1e3) / 1e9,
+            "note": "fp32 SIMT (CUDA cores); A is 2.2 GB > L2"}
 
 
 def extra_backbone(dev, world, rank):

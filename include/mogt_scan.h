@@ -125,6 +125,20 @@ int mogt_gated_scan_bwd(const void* q, const void* k, const void* v, const float
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Dense-transition headed scan:
+ *     S_t = A_t S_{t-1} + (1 - f_t) k_t v_t^T,   o_t = S_t^T q_t.
+ * Replaces affine_scan.py:14-62 (affine_scan_sequential on U = A,
+ * V = (1-f) k v^T) followed by the readout einsum.
+ *   A : [BH, T, d, d] fp32 (16-byte aligned), q, k, v, o : [BH, T, d],
+ *   f : [BH, T] fp32; S0 / S_final : [BH, d, d] fp32 or NULL; o may be NULL.
+ *   d in {16, 32, 64}; in_dtype bf16 or f32; out_dtype bf16 or f32 (f32 for
+ *   f32 inputs).  fp32 arithmetic throughout.
+ * ------------------------------------------------------------------------- */
+int mogt_matrix_scan_fwd(const float* A, const void* q, const void* k, const void* v,
+                         const float* f, void* o, const float* S0, float* S_final, int64_t BH,
+                         int64_t T, int64_t d, int in_dtype, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).
  * Replaces triton_scan.py:232-311 (_triton_affine_scan_hybrid_forward: local
  * Triton kernel + Python carry scan + carry apply), triton_scan.py:151-175

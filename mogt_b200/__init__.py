@@ -10,7 +10,15 @@ Public API:
 from . import ops, triton_scan  # noqa: F401
 from .gated import gated_scan  # noqa: F401
 
-__all__ = ["gated_scan", "ops", "triton_scan", "install_as_triton_scan"]
+
+def matrix_scan(A, q, k, v, f, *, initial_state=None, output_dtype=None):
+    """Dense-transition headed scan (forward): S_t = A_t S_{t-1} + (1-f_t) k_t v_t^T,
+    o_t = S_t^T q_t.  A: [B, H, T, d, d] fp32; q, k, v: [B, H, T, d]."""
+    o, _ = ops.matrix_scan_fwd(A, q, k, v, f, initial_state=initial_state, output_dtype=output_dtype)
+    return o
+
+
+__all__ = ["gated_scan", "matrix_scan", "ops", "triton_scan", "install_as_triton_scan"]
 
 
 def install_as_triton_scan():

@@ -11,7 +11,7 @@ import torch
 
 from . import _native as N
 
-__all__ = ["gated_scan_fwd", "gated_scan_bwd", "affine_scan", "affine_grad_u", "gated_num_segments"]
+__all__ = ["gated_scan_fwd", "gated_scan_bwd", "matrix_scan_fwd", "affine_scan", "affine_grad_u", "gated_num_segments"]
 
 
 def _require_cuda(*ts, what):
@@ -107,6 +107,34 @@ def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False):
                                    dk, dv, code, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
     N.check(st, "mogt_gated_scan_bwd")
     return gq, gk, gv, gf, gS0
+
+
+def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False):
+    """o_t = S_t^T q_t with S_t = A_t S_{t-1} + (1-f_t) k_t v_t^T (dense A_t).
+    A: [B, H, T, d, d]; q, k, v: [B, H, T, d]; f: [B, H, T]; d in {16, 32, 64}.
+    Returns (o, S_final)."""
+    _require_cuda(A, q, k, v, f, initial_state, what="matrix_scan")
+    if A.ndim != 5 or q.ndim != 4:
+        raise ValueError("A must be [B, H, T, d, d] and q, k, v [B, H, T, d]")
+    B, H, T, d = q.shape
+    if A.shape != (B, H, T, d, d) or k.shape != q.shape or v.shape != q.shape or f.shape != (B, H, T):
+        raise ValueError("A: [B, H, T, d, d]; q, k, v: [B, H, T, d]; f: [B, H, T]")
+    if q.dtype not in (torch.bfloat16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("q, k, v must share dtype bfloat16 or float32")
+    out_dtype = output_dtype or q.dtype
+    dev = q.device
+    A = A.to(torch.float32).contiguous()
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    f = f.to(torch.float32).contiguous()
+    S0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    o = torch.empty(B, H, T, d, dtype=out_dtype, device=dev)
+    S_fin = torch.empty(B, H, d, d, dtype=torch.float32, device=dev) if want_final else None
+    with torch.cuda.device(dev):
+        st = N.lib().mogt_matrix_scan_fwd(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
+                                          N.ptr(S0), N.ptr(S_fin), B * H, T, d, N.dtype_code(q.dtype),
+                                          N.dtype_code(out_dtype), N.stream_ptr(dev))
+    N.check(st, "mogt_matrix_scan_fwd")
+    return o, S_fin
 
 
 def _check_uv(U, V):
