@@ -71,17 +71,18 @@ int mogt_workspace_clear(void* workspace, size_t workspace_bytes, void* stream);
  *   S0          [BH, dk, dv] fp32 initial state, or NULL for zeros
  *   S_final     [BH, dk, dv] fp32 final state S_T, or NULL
  *   decay_final [BH] fp32 product of all f (the carry's decay), or NULL
- *   seg_states  [BH, nseg, dk, dv] fp32 state entering each segment (saved for
- *               the backward), or NULL; nseg = mogt_gated_scan_num_segments()
+ *   chunk_states [BH, nchunks, dk, dv] bf16 state entering each 64-step chunk
+ *               (saved for the backward; bf16 path only), or NULL;
+ *               nchunks = mogt_gated_scan_num_chunks()
  *   o may be NULL: only the final state / decay are produced (the first phase
  *   of the sequence-parallel scan).
  * Gates must lie in [0, 1] (the chunked path works with log2 f).
  * ------------------------------------------------------------------------- */
-int64_t mogt_gated_scan_num_segments(int64_t T, int64_t dk, int64_t dv, int in_dtype);
+int64_t mogt_gated_scan_num_chunks(int64_t T, int64_t dk, int64_t dv, int in_dtype);
 size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, int64_t dv,
                                            int in_dtype);
 int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
-                        const float* S0, float* S_final, float* decay_final, float* seg_states,
+                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
                         int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
@@ -103,7 +104,7 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
  * threads) race and must be serialised by the caller. */
 int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v, const float* f,
                                 void* o, const float* S0, float* S_final, float* decay_final,
-                                float* seg_states, int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                                void* chunk_states, int64_t BH, int64_t T, int64_t dk, int64_t dv,
                                 int in_dtype, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------

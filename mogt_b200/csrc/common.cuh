@@ -322,6 +322,25 @@ __device__ __forceinline__ void tmem_ld_16x32(float (&acc)[4][4], uint32_t taddr
     for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(r[4 * n + e]);
 }
 
+// Same load without the wait: several loads can be in flight before one
+// tmem_wait_ld(); the registers are valid only after it.
+__device__ __forceinline__ void tmem_ld_16x32_async(uint32_t (&r)[16], uint32_t taddr) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.16x256b.x4.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void frag_from_u32(float (&acc)[4][4], const uint32_t (&r)[16]) {
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[n][e] = __uint_as_float(r[4 * n + e]);
+}
+
 // Tensor-memory allocation by one full warp; the address lands in *slot.
 __device__ __forceinline__ void tmem_alloc(uint32_t* slot, uint32_t ncols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),

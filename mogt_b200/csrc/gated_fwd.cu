@@ -33,6 +33,7 @@
 // per-element form is used.  Per-step log2 gates are
 // clamped at -64 so f = 0 is a (numerically) full reset.
 #include "common.cuh"
+#include "gated_common.cuh"
 #include "gated_internal.h"
 #include "lookback.cuh"
 
@@ -61,17 +62,11 @@ __device__ __forceinline__ void trace_clk(uint32_t unit, int k) {
 namespace mogt {
 namespace gated {
 
-constexpr int D = 64;
-constexpr int CH = 64;
-constexpr int NTHREADS = 256;             // 8 warps
 constexpr int STAGES = 3;                 // pass-2 ring: q, k, v per slot
 constexpr int P1_STAGES = 5;              // pass-1 ring: k, v per slot
 constexpr int P1_AHEAD = 3;               // pass-1 chunks loading ahead
-constexpr int SEG_CHUNKS = 4;             // saved-state granularity: 256 tokens
 constexpr int MAX_CPS = 256;              // chunks per stripe (suffix table)
-constexpr int TILE = CH * D * 2;          // one 64x64 bf16 tile, 8 KB
 constexpr int SLOT = 3 * TILE;            // q, k, v of one chunk
-constexpr float kFactorMin = -100.f;      // log2 chunk decay above which D factorises
 
 constexpr int SM_RING = 0;
 constexpr int SM_SBUF = SM_RING + STAGES * SLOT;   // bf16 state operand [i][j] (+ pass-1 ring)
@@ -101,14 +96,14 @@ struct Params {
   const float* S0;
   float* S_final;
   float* decay_final;
-  float* seg_states;
+  __nv_bfloat16* chunk_states;  // [BH, nchunks, 64, 64] state entering each chunk, or null
   WsHeader* hdr;
   uint32_t* flags;
   float* a_agg;
   float* a_inc;
   float* st_agg;
   float* st_inc;
-  int T, BH, nchunks, cps, nstripes, nseg;
+  int T, BH, nchunks, cps, nstripes;
 };
 
 struct WsLayout {
@@ -147,114 +142,6 @@ inline int resident_ctas() {
   if (cudaGetDevice(&dev) == cudaSuccess)
     cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
   return 2 * nsm;
-}
-
-__device__ __forceinline__ void tma_load_3d_hint(void* dst, const CUtensorMap* map, uint64_t* bar,
-                                                 int32_t c0, int32_t c1, int32_t c2, uint64_t pol) {
-  asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2), "l"(pol)
-      : "memory");
-}
-
-__device__ __forceinline__ float clamped_log2(float f) { return fmaxf(fast_log2(f), -64.f); }
-
-// Gates of chunk gc: lane l holds steps 2l, 2l+1 (t >= T reads as "no step":
-// f = 1, so log2 f = 0 and 1 - f = 0).  Loaded one chunk ahead of use.
-__device__ __forceinline__ float2 gate_load(const float* fh, int T, int gc, int lane) {
-  const int t = gc * CH + 2 * lane;
-  float2 r;
-  r.x = t < T ? __ldg(fh + t) : 1.f;
-  r.y = t + 1 < T ? __ldg(fh + t + 1) : 1.f;
-  return r;
-}
-
-// Chunk-local gate values, held by every warp for itself: lane l owns steps
-// 2l and 2l+1 (inclusive log2 cumulative gate l, 1 - f as w); tot is the log2
-// decay of the whole chunk (all lanes).
-struct WGates {
-  float l0, l1, w0, w1, tot;
-};
-__device__ __forceinline__ WGates warp_gates(float2 fv, int lane) {
-  WGates gt;
-  const float x0 = clamped_log2(fv.x), x1 = clamped_log2(fv.y);
-  gt.w0 = 1.f - fv.x;
-  gt.w1 = 1.f - fv.y;
-  const float pair = x0 + x1;
-  float inc = pair;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const float y = __shfl_up_sync(0xffffffffu, inc, o);
-    if (lane >= o) inc += y;
-  }
-  gt.l0 = inc - pair + x0;
-  gt.l1 = inc;
-  gt.tot = __shfl_sync(0xffffffffu, inc, 31);
-  return gt;
-}
-// Value of step r (0..63) of a per-step quantity held as (v0, v1) pairs.
-__device__ __forceinline__ float step_val(float v0, float v1, int r) {
-  const float a = __shfl_sync(0xffffffffu, v0, r >> 1);
-  const float b = __shfl_sync(0xffffffffu, v1, r >> 1);
-  return (r & 1) ? b : a;
-}
-__device__ __forceinline__ bool factorises(const WGates& gt) { return gt.tot >= kFactorMin; }
-
-// Rows this thread scales when building a 64x64 tile: 4w + lane/8 and 32 + that.
-__device__ __forceinline__ int build_row(int tid, int j) { return (tid + NTHREADS * j) >> 3; }
-
-// dst rows (r, swizzled 128-byte rows) = scale_r * src rows, for this thread's
-// two rows (see build_row), 16 bytes each.
-__device__ __forceinline__ void build_rows(uint8_t* dst, const uint8_t* src, float s0, float s1,
-                                           int tid) {
-#pragma unroll
-  for (int j = 0; j < 2; ++j) {
-    const int q = tid + NTHREADS * j, row = q >> 3, chunk = q & 7;
-    const uint32_t off = sw128(row, chunk);
-    const uint4 v = *reinterpret_cast<const uint4*>(src + off);
-    const float c = j ? s1 : s0;
-    uint4 w;
-    w.x = scale_bf16x2(v.x, c, c);
-    w.y = scale_bf16x2(v.y, c, c);
-    w.z = scale_bf16x2(v.z, c, c);
-    w.w = scale_bf16x2(v.w, c, c);
-    *reinterpret_cast<uint4*>(dst + off) = w;
-  }
-}
-
-// Fragment geometry of a thread in the 8-warp layout: rows r0 and r0 + 8,
-// columns 8 * (4 hf + n) + 2 c4 (+1) for n = 0..3.
-struct Frag {
-  int r0, hf, c4;
-};
-
-__device__ __forceinline__ void store_frag_bf16(uint8_t* tile, const float (&s)[4][4], Frag fr) {
-#pragma unroll
-  for (int n = 0; n < 4; ++n) {
-    const uint32_t chunk = 4 * fr.hf + n, col = 4u * fr.c4;
-    *reinterpret_cast<uint32_t*>(tile + sw128(fr.r0, chunk) + col) = pack_bf16(s[n][0], s[n][1]);
-    *reinterpret_cast<uint32_t*>(tile + sw128(fr.r0 + 8, chunk) + col) = pack_bf16(s[n][2], s[n][3]);
-  }
-}
-
-__device__ __forceinline__ void store_frag_rowmajor(float* dst, const float (&s)[4][4], Frag fr) {
-#pragma unroll
-  for (int n = 0; n < 4; ++n) {
-    const int j = 8 * (4 * fr.hf + n) + 2 * fr.c4;
-    *reinterpret_cast<float2*>(dst + fr.r0 * D + j) = make_float2(s[n][0], s[n][1]);
-    *reinterpret_cast<float2*>(dst + (fr.r0 + 8) * D + j) = make_float2(s[n][2], s[n][3]);
-  }
-}
-
-__device__ __forceinline__ void load_frag_rowmajor(float (&s)[4][4], const float* src, Frag fr) {
-#pragma unroll
-  for (int n = 0; n < 4; ++n) {
-    const int j = 8 * (4 * fr.hf + n) + 2 * fr.c4;
-    const float2 lo = __ldg(reinterpret_cast<const float2*>(src + fr.r0 * D + j));
-    const float2 hi = __ldg(reinterpret_cast<const float2*>(src + (fr.r0 + 8) * D + j));
-    s[n][0] = lo.x; s[n][1] = lo.y; s[n][2] = hi.x; s[n][3] = hi.y;
-  }
 }
 
 template <bool OUT_F32>
@@ -304,7 +191,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   const int nc = min(p.cps, p.nchunks - c_begin);
   const bool has_succ = stripe + 1 < p.nstripes;
   const bool want_out = p.o != nullptr;
-  const bool need_p2 = want_out || p.seg_states != nullptr;
+  const bool need_p2 = want_out || p.chunk_states != nullptr;
   const bool need_p1 = has_succ || !need_p2;
   const int n1 = need_p1 ? nc : 0;
   const int nit = n1 + (need_p2 ? nc : 0);
@@ -534,10 +421,10 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         umma_commit(bar_m3);
       }
     };
-    auto write_out = [&](int c) {
-      // output rows of chunk c from the O buffer of chunk c
+    auto write_out_regs = [&](int c, const uint32_t (&r)[16]) {
+      // output rows of chunk c from its O accumulator (already loaded)
       float oacc[4][4];
-      tmem_ld_16x32(oacc, tw + TM_O0 + 64u * (c & 1));
+      frag_from_u32(oacc, r);
       const int ta = (gc0 + c) * CH + fr.r0, tb = ta + 8;
       const size_t rowa = ((size_t)bh * T + ta) * D, rowb = ((size_t)bh * T + tb) * D;
 #pragma unroll
@@ -555,8 +442,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
     };
 
-    if (p.seg_states && (gc0 % SEG_CHUNKS) == 0)
-      store_frag_rowmajor(p.seg_states + ((size_t)bh * p.nseg + gc0 / SEG_CHUNKS) * D * D, sin, fr);
+    if (p.chunk_states)
+      store_frag_rowmajor_bf16(p.chunk_states + ((size_t)bh * p.nchunks + gc0) * D * D, sin, fr);
     store_frag_bf16(s_tile, sin, fr);
     if (!mbar_wait(&bars[0], 0)) ok = false;
     build_chunk(0, gcur);
@@ -569,19 +456,37 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     for (int c = 0; c < nc; ++c) {
       const int it = n1 + c;
       const bool fast = factorises(gcur);
+      // gates of chunk c+1: independent of the MMAs in flight
+      WGates gnext = gcur;
+      if (c + 1 < nc) {
+        gnext = warp_gates(fnext, lane);
+        if (c + 2 < nc) fnext = gate_load(fh, T, gc0 + c + 2, lane);
+      }
       MOGT_CLK(unit, 5, c == 5);
       wait_bar(bar_m1, ph_m1);
       ph_m1 ^= 1u;
       wait_bar(bar_m3, ph_m3);
       ph_m3 ^= 1u;
+      if (c > 0) {
+        wait_bar(bar_m2, ph_m2);
+        ph_m2 ^= 1u;
+      }
       tc_fence_after();
       MOGT_CLK(unit, 6, c == 5);
+      // all tensor-memory reads of this iteration in flight together
+      const bool need_ds = c + 1 < nc || (final_here && p.S_final);
+      uint32_t r_ds[16], r_p[16], r_o[16];
+      if (need_ds) tmem_ld_16x32_async(r_ds, tw + TM_DS);
+      if (want_out) tmem_ld_16x32_async(r_p, tw + TM_P);
+      if (want_out && c > 0) tmem_ld_16x32_async(r_o, tw + TM_O0 + 64u * ((c - 1) & 1));
+      tmem_wait_ld();
+      MOGT_CLK(unit, 14, c == 5);
       // state for chunk c+1 (or the final state)
       const float dC = fast_exp2(gcur.tot);
       ltot2 += gcur.tot;
-      if (c + 1 < nc || (final_here && p.S_final)) {
+      if (need_ds) {
         float ds[4][4];
-        tmem_ld_16x32(ds, tw + TM_DS);
+        frag_from_u32(ds, r_ds);
         if (fast) {
 #pragma unroll
           for (int n = 0; n < 4; ++n)
@@ -595,23 +500,18 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         }
         if (c + 1 < nc) {
           store_frag_bf16(s_tile, sin, fr);
-          const int gn = gc0 + c + 1;
-          if (p.seg_states && (gn % SEG_CHUNKS) == 0)
-            store_frag_rowmajor(p.seg_states + ((size_t)bh * p.nseg + gn / SEG_CHUNKS) * D * D, sin, fr);
+          if (p.chunk_states)
+            store_frag_rowmajor_bf16(p.chunk_states + ((size_t)bh * p.nchunks + gc0 + c + 1) * D * D, sin, fr);
         }
       }
+      MOGT_CLK(unit, 15, c == 5);
       // output of the previous chunk
-      if (c > 0) {
-        wait_bar(bar_m2, ph_m2);
-        ph_m2 ^= 1u;
-        tc_fence_after();
-        if (want_out) write_out(c - 1);
-      }
+      if (want_out && c > 0) write_out_regs(c - 1, r_o);
       MOGT_CLK(unit, 7, c == 5);
       // P'_c: causal mask (and the exact decays when they do not factorise)
       if (want_out) {
         float pacc[4][4];
-        tmem_ld_16x32(pacc, tw + TM_P);
+        frag_from_u32(pacc, r_p);
         const int tl0 = fr.r0, tl1 = tl0 + 8;
         if (fast) {
 #pragma unroll
@@ -638,10 +538,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
       MOGT_CLK(unit, 8, c == 5);
       // operands of chunk c+1
-      WGates gnext = gcur;
       if (c + 1 < nc) {
-        gnext = warp_gates(fnext, lane);
-        if (c + 2 < nc) fnext = gate_load(fh, T, gc0 + c + 2, lane);
         if (!mbar_wait(&bars[(c + 1) % STAGES], ((c + 1) / STAGES) & 1)) ok = false;
         build_chunk(c + 1, gnext);
       }
@@ -670,7 +567,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     wait_bar(bar_m2, ph_m2);
     ph_m2 ^= 1u;
     tc_fence_after();
-    if (want_out) write_out(nc - 1);
+    if (want_out) {
+      uint32_t r_o[16];
+      tmem_ld_16x32_async(r_o, tw + TM_O0 + 64u * ((nc - 1) & 1));
+      tmem_wait_ld();
+      write_out_regs(nc - 1, r_o);
+    }
     if (final_here) {
       if (p.S_final) store_frag_rowmajor(p.S_final + (size_t)bh * D * D, sin, fr);
       if (tid == 0 && p.decay_final) p.decay_final[bh] = a_in * fast_exp2(ltot2);
@@ -704,9 +606,9 @@ int mogt_debug_set_trace(void* buf) {
 }
 #endif
 
-int64_t mogt_gated_scan_num_segments(int64_t T, int64_t dk, int64_t dv, int in_dtype) {
+int64_t mogt_gated_scan_num_chunks(int64_t T, int64_t dk, int64_t dv, int in_dtype) {
   if (in_dtype != MOGT_DTYPE_BF16 || dk != D || dv != D || T <= 0) return 0;
-  return (T + SEG_CHUNKS * CH - 1) / (SEG_CHUNKS * CH);
+  return (T + CH - 1) / CH;
 }
 
 size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, int64_t dv,
@@ -718,7 +620,7 @@ size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
 }
 
 int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
-                        const float* S0, float* S_final, float* decay_final, float* seg_states,
+                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
                         int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
                         void* workspace, size_t workspace_bytes, void* stream) {
   if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
@@ -728,7 +630,7 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (in_dtype == MOGT_DTYPE_F32) {
     if (out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
-    if (seg_states) return MOGT_ERR_UNSUPPORTED;
+    if (chunk_states) return MOGT_ERR_UNSUPPORTED;
     return launch_fwd_seq(static_cast<const float*>(q), static_cast<const float*>(k),
                           static_cast<const float*>(v), f, static_cast<float*>(o), S0, S_final,
                           decay_final, (int)BH, (int)T, (int)dk, (int)dv, s);
@@ -763,7 +665,7 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   P.S0 = S0;
   P.S_final = S_final;
   P.decay_final = decay_final;
-  P.seg_states = seg_states;
+  P.chunk_states = static_cast<__nv_bfloat16*>(chunk_states);
   P.hdr = reinterpret_cast<WsHeader*>(ws);
   P.flags = reinterpret_cast<uint32_t*>(ws + L.flags);
   P.a_agg = reinterpret_cast<float*>(ws + L.a_agg);
@@ -775,7 +677,6 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   P.nchunks = pl.nchunks;
   P.cps = pl.cps;
   P.nstripes = pl.nstripes;
-  P.nseg = (int)mogt_gated_scan_num_segments(T, dk, dv, in_dtype);
   if (out_dtype == MOGT_DTYPE_F32) {
     cudaFuncSetAttribute(gated_fwd_stripe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC);
     gated_fwd_stripe<true><<<(unsigned)NU, NTHREADS, SM_ALLOC, s>>>(maps[0], maps[1], maps[2], P);
@@ -824,7 +725,7 @@ void* static_scratch_for_current_device() {
 
 extern "C" int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v,
                                            const float* f, void* o, const float* S0,
-                                           float* S_final, float* decay_final, float* seg_states,
+                                           float* S_final, float* decay_final, void* chunk_states,
                                            int64_t BH, int64_t T, int64_t dk, int64_t dv,
                                            int in_dtype, int out_dtype, void* stream) {
   if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
@@ -842,6 +743,6 @@ extern "C" int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const v
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (clear_bytes && cudaMemsetAsync(scratch, 0, clear_bytes, s) != cudaSuccess)
     return MOGT_ERR_LAUNCH;
-  return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, seg_states, BH, T, dk, dv,
+  return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk, dv,
                              in_dtype, out_dtype, scratch, kStaticScratchBytes, stream);
 }

@@ -11,7 +11,7 @@ import torch
 
 from . import _native as N
 
-__all__ = ["gated_scan_fwd", "gated_scan_bwd", "matrix_scan_fwd", "affine_scan", "affine_grad_u", "gated_num_segments"]
+__all__ = ["gated_scan_fwd", "gated_scan_bwd", "matrix_scan_fwd", "affine_scan", "affine_grad_u", "gated_num_chunks"]
 
 
 def _require_cuda(*ts, what):
@@ -20,8 +20,8 @@ def _require_cuda(*ts, what):
             raise ValueError(f"{what} requires CUDA tensors")
 
 
-def gated_num_segments(T: int, dk: int, dv: int, dtype: torch.dtype) -> int:
-    return int(N.lib().mogt_gated_scan_num_segments(T, dk, dv, N.dtype_code(dtype)))
+def gated_num_chunks(T: int, dk: int, dv: int, dtype: torch.dtype) -> int:
+    return int(N.lib().mogt_gated_scan_num_chunks(T, dk, dv, N.dtype_code(dtype)))
 
 
 def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False,
@@ -31,7 +31,9 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     q, k: [B, H, T, dk]; v: [B, H, T, dv]; f: [B, H, T] (any float dtype, used
     as fp32).  bf16 inputs take the tensor-core path (dk = dv = 64); fp32
     inputs take the exact sequential path.  Returns (o, S_final, decay_final,
-    seg_states) with the optional members None unless requested.
+    chunk_states) with the optional members None unless requested;
+    chunk_states [B, H, ceil(T/64), dk, dv] bf16 holds the state entering each
+    64-step chunk (bf16 path only).
     """
     _require_cuda(q, k, v, f, initial_state, what="gated_scan")
     if k.ndim != 4 or v.ndim != 4 or f.ndim != 3 or (q is not None and q.ndim != 4):
@@ -62,9 +64,9 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     dec = torch.empty(B, H, dtype=torch.float32, device=dev) if want_final else None
     seg = None
     if save_states:
-        nseg = gated_num_segments(T, dk, dv, in_dtype)
-        if nseg > 0:
-            seg = torch.empty(B, H, nseg, dk, dv, dtype=torch.float32, device=dev)
+        nch = gated_num_chunks(T, dk, dv, in_dtype)
+        if nch > 0:
+            seg = torch.empty(B, H, nch, dk, dv, dtype=torch.bfloat16, device=dev)
     L = N.lib()
     icode, ocode = N.dtype_code(in_dtype), N.dtype_code(out_dtype)
     nbytes = L.mogt_gated_scan_fwd_workspace_bytes(BH, T, dk, dv, icode)

@@ -34,8 +34,8 @@ def test_library_exports_every_declared_symbol():
 def test_workspace_sizes_without_gpu():
     from mogt_b200 import _native
     lib = _native.lib()
-    assert lib.mogt_gated_scan_num_segments(32768, 64, 64, _native.BF16) == 128
-    assert lib.mogt_gated_scan_num_segments(32768, 64, 64, _native.F32) == 0
+    assert lib.mogt_gated_scan_num_chunks(32768, 64, 64, _native.BF16) == 512
+    assert lib.mogt_gated_scan_num_chunks(32768, 64, 64, _native.F32) == 0
     ws = lib.mogt_gated_scan_fwd_workspace_bytes(12, 32768, 64, 64, _native.BF16)
     assert ws >= 12 * 2 * 64 * 64 * 4  # at least one stripe state pair per head
     assert lib.mogt_affine_scan_workspace_bytes(1, 32768, 16, 48) > 0

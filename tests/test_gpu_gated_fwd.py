@@ -70,20 +70,20 @@ def test_fp32_initial_and_final_state(mg):
     assert rel_max_err(S_fin.cpu().numpy(), Sref) <= TOL_F32
 
 
-def test_segment_states_and_state_only_mode(mg):
+def test_chunk_states_and_state_only_mode(mg):
     m, _ = mg
     T = 1100
     q, k, v, f = headed_bf16(1, 2, T, seed=11)
     o, S_fin, dec, seg = m.ops.gated_scan_fwd(q.cuda(), k.cuda(), v.cuda(), f.cuda(),
                                               want_final=True, save_states=True)
-    assert seg.shape == (1, 2, 5, 64, 64)
-    # state entering segment s is S_{256 s - 1}
+    assert seg.shape == (1, 2, 18, 64, 64) and seg.dtype == torch.bfloat16
+    # state entering chunk c is S_{64 c - 1} (bf16-rounded)
     kk, vv, ff = as64(k, v, f)
     S = np.zeros((2, 64, 64))
     assert float(seg[0, :, 0].abs().max()) == 0.0
     for t in range(T):
-        if t % 256 == 0 and t > 0:
-            assert rel_max_err(seg[0, :, t // 256].cpu().numpy(), S) <= TOL_BF16
+        if t % 64 == 0 and t > 0:
+            assert rel_max_err(seg[0, :, t // 64].float().cpu().numpy(), S) <= TOL_BF16
         S = ff[0, :, t, None, None] * S + (1 - ff[0, :, t, None, None]) * kk[0, :, t, :, None] * vv[0, :, t, None, :]
     assert rel_max_err(S_fin[0].cpu().numpy(), S) <= TOL_BF16
     # state-only (first phase of the sequence-parallel scan): no q, no o
