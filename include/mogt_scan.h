@@ -116,13 +116,18 @@ int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v, con
  *   inputs as mogt_gated_scan_fwd, d_o : [BH, T, dv] (same dtype as q)
  *   dq, dk : [BH, T, dk], dv : [BH, T, dv] in the input dtype; df : [BH, T] fp32
  *   dS0 : [BH, dk, dv] fp32 gradient of the initial state S0, or NULL
- *   in_dtype MOGT_DTYPE_F32: exact sequential kernels (dk, dv <= 128).
+ *   in_dtype MOGT_DTYPE_F32: exact sequential kernels (dk, dv <= 128); S0 is
+ *     the forward's initial state (or NULL), chunk_states must be NULL.
+ *   in_dtype MOGT_DTYPE_BF16 (dk = dv = 64): reverse-time chunked tensor-core
+ *     kernel; chunk_states = the bf16 per-chunk states written by
+ *     mogt_gated_scan_fwd on the same inputs (they already hold S0, which is
+ *     ignored); all bf16 pointers 16-byte aligned.
  * ------------------------------------------------------------------------- */
 size_t mogt_gated_scan_bwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, int64_t dv,
                                            int in_dtype);
 int mogt_gated_scan_bwd(const void* q, const void* k, const void* v, const float* f,
-                        const void* d_o, const float* S0, void* dq, void* dk, void* dv, float* df,
-                        float* dS0, int64_t BH, int64_t T, int64_t dk_, int64_t dv_, int in_dtype,
+                        const void* d_o, const float* S0, const void* chunk_states, void* dq,
+                        void* dk, void* dv, float* df, float* dS0, int64_t BH, int64_t T, int64_t dk_, int64_t dv_, int in_dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------

@@ -198,6 +198,11 @@ int launch_bwd_seq_t(const float* q, const float* k, const float* v, const float
   return mogt_host::launch_status();
 }
 
+size_t bwd_tc_workspace_bytes(int64_t BH, int64_t T);
+int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, const void* d_o,
+                  const void* chunk_states, void* dq, void* dk, void* dv, float* df, float* dS0,
+                  int BH, int T, void* workspace, size_t workspace_bytes, cudaStream_t s);
+
 size_t bwd_seq_workspace_bytes(int64_t BH, int64_t T, int64_t dk, int64_t dv) {
   const size_t nch = (size_t)(T + BWD_CHUNK - 1) / BWD_CHUNK;
   return (size_t)BH * (nch + BWD_CHUNK) * dk * dv * sizeof(float);
@@ -215,19 +220,30 @@ size_t mogt_gated_scan_bwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
                                            int in_dtype) {
   if (BH <= 0 || T <= 0 || dk <= 0 || dv <= 0) return 0;
   if (in_dtype == MOGT_DTYPE_F32) return bwd_seq_workspace_bytes(BH, T, dk, dv);
+  if (in_dtype == MOGT_DTYPE_BF16 && dk == 64 && dv == 64) return bwd_tc_workspace_bytes(BH, T);
   return 0;
 }
 
 int mogt_gated_scan_bwd(const void* q, const void* k, const void* v, const float* f,
-                        const void* d_o, const float* S0, void* dq, void* dk, void* dv, float* df,
-                        float* dS0, int64_t BH, int64_t T, int64_t dk_, int64_t dv_, int in_dtype,
+                        const void* d_o, const float* S0, const void* chunk_states, void* dq,
+                        void* dk, void* dv, float* df, float* dS0, int64_t BH, int64_t T, int64_t dk_, int64_t dv_, int in_dtype,
                         void* workspace, size_t workspace_bytes, void* stream) {
   if (BH <= 0 || T < 0 || dk_ <= 0 || dv_ <= 0) return MOGT_ERR_SHAPE;
   if (T == 0) return MOGT_OK;
   if (!q || !k || !v || !f || !d_o || !dq || !dk || !dv || !df) return MOGT_ERR_ARG;
   if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (in_dtype == MOGT_DTYPE_BF16) {
+    if (dk_ != 64 || dv_ != 64) return MOGT_ERR_UNSUPPORTED;
+    if (!chunk_states) return MOGT_ERR_ARG;
+    const void* ptrs[8] = {q, k, v, d_o, chunk_states, dq, dk, dv};
+    for (const void* p : ptrs)
+      if ((reinterpret_cast<uintptr_t>(p) & 15u) != 0) return MOGT_ERR_ALIGN;
+    return launch_bwd_tc(q, k, v, f, d_o, chunk_states, dq, dk, dv, df, dS0, (int)BH, (int)T,
+                         workspace, workspace_bytes, s);
+  }
   if (in_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+  if (chunk_states) return MOGT_ERR_ARG;
   if (dk_ > 128 || dv_ > 128) return MOGT_ERR_UNSUPPORTED;
   if (!workspace || workspace_bytes < bwd_seq_workspace_bytes(BH, T, dk_, dv_)) return MOGT_ERR_WORKSPACE;
   const float *qf = static_cast<const float*>(q), *kf = static_cast<const float*>(k),

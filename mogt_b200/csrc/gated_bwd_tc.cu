@@ -1,0 +1,741 @@
+// Headed gated scan, backward on tensor cores (bf16 q/k/v/do, dk = dv = 64).
+//
+// Forward:  S_t = f_t S_{t-1} + w_t k_t v_t^T  (w = 1 - f),  o_t = S_t^T q_t.
+// Adjoint:  G_t = q_t do_t^T + f_{t+1} G_{t+1};
+//   dq_t = S_t do_t,  dk_t = w_t G_t v_t,  dv_t = w_t G_t^T k_t,
+//   df_t = <G_t, S_{t-1}> - k_t^T G_t v_t,  dS_0 = f_0 G_0
+// (the chain rule through affine_scan.py:65-124 with U_t = f_t I and
+// V_t = w_t k_t v_t^T; same quantities as the sequential kernel).
+//
+// Reverse-time chunked scan.  Chunk = 64 steps with chunk-local inclusive
+// log2 cumulative gates l_t (L = l_63), X = the adjoint carry entering the
+// chunk from the later ones (G_63 = q_63 do_63^T + X), S_in = the state
+// entering the chunk, read from the bf16 per-chunk states the forward saved.
+// With decays d[u,s] = exp2(l_u - l_s) (u >= s):
+//   M1 = dO V^T, PQ = Q K^T, M1d = d o M1, PQd = d o PQ (lower incl. diag),
+//   dq = diag(exp2 l) dO S_in^T + M1d (diag(w) K)
+//   dk = diag(w) [M1d^T Q + diag(exp2(L - l)) V X^T]
+//   dv = diag(w) [PQd^T dO + diag(exp2(L - l)) K X]
+//   X_prev = exp2(L) X + (diag(exp2 l) Q)^T dO        (carry into the chunk before)
+// and df_t from four product terms, none of which cancels:
+//   <G_t, S_{t-1}> = exp2(L - x_t) <X, S_in>                  x_t = l_t - l_{t-1}
+//                  + exp2(l_{t-1}) R_t,  R_t = z_t + f_{t+1} R_{t+1},  z_u = q_u^T S_in do_u
+//                  + exp2(L - l_t) P_{t-1},  P_t = f_t P_{t-1} + w_t y_t,  y_s = k_s^T X v_s
+//                  + exp2(-x_t) sum_{u >= t > s} d[u,s] w_s (q_u.k_s)(do_u.v_s)
+//   k_t^T G_t v_t  = k_t.(M1d^T Q)_t + exp2(L - l_t) y_t.
+// Every decay is formed per element from differences of l, so the form is
+// exact for any gates (no factorisation condition, no fallback path).
+//
+// Work decomposition mirrors the forward: the chunks of a head are cut into
+// stripes; a CTA (8 warps, one per SM) owns a stripe and runs
+//   pass 1  the stripe's carry aggregate  sum_c exp2(lpre_c) Q^_c^T dO_c
+//           (lpre = log2 decay of the stripe's chunks before c) in tensor
+//           memory, published for the stripe before it;
+//   look-back  over the later stripes of the head (windowed, decoupled) for
+//           the carry entering the stripe's end;
+//   pass 2  the chunks in reverse order: 9 tcgen05 MMAs per chunk (6 of the
+//           carry and the raw tiles, 3 of the masked products), epilogues
+//           in registers, and one warp forms df from per-step partial sums.
+#include "common.cuh"
+#include "gated_common.cuh"
+#include "lookback.cuh"
+
+namespace mogt {
+namespace gated {
+namespace bwd {
+
+constexpr int STAGES = 3;                  // pass-2 ring: q, k, v, do, S_in per slot
+constexpr int P1_STAGES = 7;               // pass-1 ring: q, do per slot
+constexpr int P1_AHEAD = 5;
+constexpr int SLOT = 5 * TILE;
+constexpr int T_Q = 0, T_K = 1, T_V = 2, T_DO = 3, T_S = 4;
+
+constexpr int SM_RING = 0;
+constexpr int SM_QH = SM_RING + STAGES * SLOT;     // diag(exp2 l) Q, [t][i]
+constexpr int SM_KW = SM_QH + TILE;                // diag(w) K, [s][i]
+constexpr int SM_X = SM_KW + TILE;                 // bf16 carry X, [i][j]
+constexpr int SM_M1 = SM_X + TILE;                 // M1d, [u][s]
+constexpr int SM_PQ = SM_M1 + TILE;                // PQd, [u][s]
+constexpr int SM_GL = SM_PQ + TILE;                // l_t of the chunk [64]
+constexpr int SM_GW = SM_GL + 256;                 // w_t [64]
+constexpr int SM_LPRE = SM_GW + 256;               // pass-1 prefix decays [MAX_CPS]
+constexpr int SM_ROWZ = SM_LPRE + MAX_CPS * 4;     // [2][64] halves of z_u
+constexpr int SM_ROWY = SM_ROWZ + 512;             // [2][64] halves of y_s
+constexpr int SM_ROWK = SM_ROWY + 512;             // [2][64] halves of k.(M1d^T Q)
+constexpr int SM_COLW = SM_ROWK + 512;             // [4][64] column sums of the E prefix
+constexpr int SM_ROWT = SM_COLW + 1024;            // [64] row totals of E, columns 0..31
+constexpr int SM_SIG = SM_ROWT + 256;              // [8] <X, S_in> per warp
+constexpr int SM_MISC = SM_SIG + 64;               // ticket, look-back scratch
+constexpr int NBARS = STAGES + P1_STAGES + 2 + 5;
+constexpr int SM_BAR = SM_MISC + 256;
+constexpr int SM_TSLOT = SM_BAR + 8 * NBARS;
+constexpr int SM_TOTAL = SM_TSLOT + 16;
+constexpr int SM_ALLOC = SM_TOTAL + 1024;
+static_assert(SM_ALLOC <= 227 * 1024, "shared memory per CTA");
+static_assert(P1_STAGES * 2 * TILE <= SM_QH - SM_RING, "pass-1 ring fits");
+
+// tensor memory (fp32 M = 64 accumulators): group-1 products, then the
+// group-2 products reuse the M1 / PQ columns once those are read
+constexpr uint32_t TMEM_COLS = 512;
+constexpr uint32_t TM_M1 = 0, TM_PQ = 64, TM_DOS = 128, TM_DX = 192, TM_VX = 256, TM_KX = 320,
+                   TM_DV2 = 384, TM_AGG = 448;
+constexpr uint32_t TM_DQ2 = TM_M1, TM_DK2 = TM_PQ;
+
+struct Params {
+  const float* f;
+  __nv_bfloat16* dq;
+  __nv_bfloat16* dk;
+  __nv_bfloat16* dv;
+  float* df;
+  float* dS0;
+  WsHeader* hdr;
+  uint32_t* flags;
+  float* a_agg;
+  float* a_inc;
+  float* st_agg;
+  float* st_inc;
+  int T, BH, nchunks, cps, nstripes;
+};
+
+__device__ __forceinline__ void zero44(float (&a)[4][4]) {
+#pragma unroll
+  for (int n = 0; n < 4; ++n)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[n][e] = 0.f;
+}
+
+// Sum over the 4 lanes of a quad (same fragment row, the four c4 lanes).
+__device__ __forceinline__ float quad_sum(float x) {
+  x += __shfl_xor_sync(0xffffffffu, x, 1);
+  x += __shfl_xor_sync(0xffffffffu, x, 2);
+  return x;
+}
+
+// dst (bf16, row-major [T][64]) rows of chunk gc from a fragment, rows >= T skipped
+__device__ __forceinline__ void store_rows_bf16(__nv_bfloat16* dst, int bh, int T, int gc,
+                                                const float (&s)[4][4], Frag fr) {
+  uint32_t* d32 = reinterpret_cast<uint32_t*>(dst);
+  const int ta = gc * CH + fr.r0, tb = ta + 8;
+  const size_t rowa = ((size_t)bh * T + ta) * D, rowb = ((size_t)bh * T + tb) * D;
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const int j = 8 * (4 * fr.hf + n) + 2 * fr.c4;
+    if (ta < T) __stcs(d32 + (rowa + j) / 2, pack_bf16(s[n][0], s[n][1]));
+    if (tb < T) __stcs(d32 + (rowb + j) / 2, pack_bf16(s[n][2], s[n][3]));
+  }
+}
+
+__global__ void __launch_bounds__(NTHREADS, 1)
+    gated_bwd_stripe(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                     const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                     const __grid_constant__ CUtensorMap ts, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hf = warp >> 2, g = lane >> 2, c4 = lane & 3;
+  const Frag fr{qd * 16 + g, hf, c4};
+  const int br0 = build_row(tid, 0), br1 = build_row(tid, 1);
+  float* sgl = reinterpret_cast<float*>(smem + SM_GL);
+  float* sgw = reinterpret_cast<float*>(smem + SM_GW);
+  float* lpre = reinterpret_cast<float*>(smem + SM_LPRE);
+  float* rowZ = reinterpret_cast<float*>(smem + SM_ROWZ);
+  float* rowY = reinterpret_cast<float*>(smem + SM_ROWY);
+  float* rowK = reinterpret_cast<float*>(smem + SM_ROWK);
+  float* colW = reinterpret_cast<float*>(smem + SM_COLW);
+  float* rowT = reinterpret_cast<float*>(smem + SM_ROWT);
+  float* sig = reinterpret_cast<float*>(smem + SM_SIG);
+  volatile uint32_t* bc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
+  uint64_t* bars1 = bars + STAGES;
+  uint64_t* bar_k = bars1 + P1_STAGES;      // pass-1 MMA commits (2)
+  uint64_t* bar_a = bar_k + 2;              // M1, PQ
+  uint64_t* bar_b = bar_k + 3;              // dO S_in^T, Q^^T dO
+  uint64_t* bar_c = bar_k + 4;              // V X^T, K X
+  uint64_t* bar_d = bar_k + 5;              // M1d (w K)
+  uint64_t* bar_e = bar_k + 6;              // M1d^T Q, PQd^T dO
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM_TSLOT);
+  uint8_t* qh_tile = smem + SM_QH;
+  uint8_t* kw_tile = smem + SM_KW;
+  uint8_t* x_tile = smem + SM_X;
+  uint8_t* m1_tile = smem + SM_M1;
+  uint8_t* pq_tile = smem + SM_PQ;
+
+  if (warp == 0) tmem_alloc(tslot, TMEM_COLS);
+  if (tid == 0) {
+    uint32_t epoch;
+    bc[0] = take_ticket(p.hdr, &epoch);
+    bc[1] = epoch;
+#pragma unroll
+    for (int s = 0; s < NBARS; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t tw = tbase + ((uint32_t)(32 * qd) << 16) + 32u * hf;
+  const uint32_t unit = bc[0], epoch = bc[1];
+  const int BH = p.BH, T = p.T;
+  // tickets run over the chain of each head from its last stripe backwards
+  const int ci = (int)unit / BH, bh = (int)unit % BH;
+  const int stripe = p.nstripes - 1 - ci;
+  const int c_begin = stripe * p.cps;
+  const int nc = min(p.cps, p.nchunks - c_begin);
+  const bool has_succ = stripe > 0;   // an earlier stripe waits for this carry
+  const int n1 = has_succ ? nc : 0;
+  const int nit = n1 + nc;
+  const float* fh = p.f + (size_t)bh * T;
+  uint32_t ph_a = 0, ph_b = 0, ph_c = 0, ph_d = 0, ph_e = 0;
+  bool ok = true;
+
+  uint64_t pol_keep = 0, pol_stream = 0;
+  if (tid == 0) {
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_keep));
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_stream));
+  }
+  // TMA loads of pipeline iteration `it`: pass 1 chunks c_begin.. forward
+  // (q, do), then pass 2 chunks in reverse (q, k, v, do, S_in)
+  auto issue = [&](int it) {
+    if (it >= nit) return;
+    if (it < n1) {
+      const int t0 = (c_begin + it) * CH;
+      const int slot = it % P1_STAGES;
+      uint8_t* base = smem + SM_RING + slot * 2 * TILE;
+      mbar_arrive_expect_tx(&bars1[slot], 2 * TILE);
+      tma_load_3d_hint(base, &tq, &bars1[slot], 0, t0, bh, pol_keep);
+      tma_load_3d_hint(base + TILE, &tdo, &bars1[slot], 0, t0, bh, pol_keep);
+    } else {
+      const int j = it - n1, slot = j % STAGES;
+      const int gc = c_begin + nc - 1 - j, t0 = gc * CH;
+      uint8_t* base = smem + SM_RING + slot * SLOT;
+      mbar_arrive_expect_tx(&bars[slot], 5 * TILE);
+      tma_load_3d_hint(base + T_Q * TILE, &tq, &bars[slot], 0, t0, bh, pol_stream);
+      tma_load_3d_hint(base + T_K * TILE, &tk, &bars[slot], 0, t0, bh, pol_stream);
+      tma_load_3d_hint(base + T_V * TILE, &tv, &bars[slot], 0, t0, bh, pol_stream);
+      tma_load_3d_hint(base + T_DO * TILE, &tdo, &bars[slot], 0, t0, bh, pol_stream);
+      tma_load_3d_hint(base + T_S * TILE, &ts, &bars[slot], 0, t0, bh, pol_stream);
+    }
+  };
+  auto wait_bar = [&](uint64_t* bar, uint32_t& ph) {
+    if (!mbar_wait(bar, ph)) ok = false;
+    ph ^= 1u;
+  };
+
+  if (tid == 0) {
+    if (n1 > 0)
+      for (int it = 0; it < P1_AHEAD && it < n1; ++it) issue(it);
+    else
+      for (int it = 0; it < STAGES - 1; ++it) issue(it);
+  }
+
+  // ---------------- pass 1: the stripe's carry aggregate ----------------
+  float agg[4][4];
+  zero44(agg);
+  float ltot = 0.f;
+  if (n1 > 0) {
+    // lpre[c] = log2 decay of the stripe's chunks before c
+    for (int c = warp; c < n1; c += NTHREADS / 32) {
+      const float2 fv = gate_load(fh, T, c_begin + c, lane);
+      float x = clamped_log2(fv.x) + clamped_log2(fv.y);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+      if (lane == 0) lpre[c] = x;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      const int per = (n1 + 31) / 32, c0 = lane * per, c1 = min(c0 + per, n1);
+      float part = 0.f;
+      for (int c = c0; c < c1; ++c) part += lpre[c];
+      float inc = part;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      if (lane == 31) bc[2] = __float_as_uint(inc);
+      float run = inc - part;
+      for (int c = c0; c < c1; ++c) {
+        const float x = lpre[c];
+        lpre[c] = run;
+        run += x;
+      }
+    }
+    __syncthreads();
+    float2 fnext = gate_load(fh, T, c_begin, lane);
+    for (int c = 0; c < n1; ++c) {
+      const WGates gt = warp_gates(fnext, lane);
+      if (c + 1 < n1) fnext = gate_load(fh, T, c_begin + c + 1, lane);
+      if (c >= 2) {
+        uint32_t ph = ((c - 2) >> 1) & 1;
+        if (!mbar_wait(&bar_k[c & 1], ph)) ok = false;
+      }
+      if (tid == 0 && c + P1_AHEAD < n1) issue(c + P1_AHEAD);
+      if (!mbar_wait(&bars1[c % P1_STAGES], (c / P1_STAGES) & 1)) ok = false;
+      const float sc = lpre[c];
+      const float e0 = fast_exp2(sc + gt.l0), e1 = fast_exp2(sc + gt.l1);
+      uint8_t* base = smem + SM_RING + (c % P1_STAGES) * 2 * TILE;
+      uint8_t* qt = (c & 1) ? kw_tile : qh_tile;
+      build_rows(qt, base, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+      fence_proxy_async();
+      tc_fence_before();
+      __syncthreads();
+      if (tid == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_AGG, smem_u32(qt), true, smem_u32(base + TILE), true, c > 0);
+        umma_commit(&bar_k[c & 1]);
+      }
+      __syncwarp();
+    }
+    {
+      uint32_t ph = ((n1 - 1) >> 1) & 1;
+      if (!mbar_wait(&bar_k[(n1 - 1) & 1], ph)) ok = false;
+    }
+    tc_fence_after();
+    tmem_ld_16x32(agg, tw + TM_AGG);
+    tc_fence_before();
+    ltot = __uint_as_float(bc[2]);
+    __syncthreads();  // pass 1 has released the ring
+    if (tid == 0)
+      for (int it = n1; it < n1 + STAGES - 1; ++it) issue(it);
+  }
+  const float A_agg = fast_exp2(ltot);
+  const size_t st_off = (size_t)unit * (D * D) + (size_t)tid * 16;
+  if (n1 > 0 && ci > 0) {
+    float4* dst = reinterpret_cast<float4*>(p.st_agg + st_off);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) __stcg(dst + n, make_float4(agg[n][0], agg[n][1], agg[n][2], agg[n][3]));
+    if (tid == 0) __stcg(p.a_agg + unit, A_agg);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release_u32(p.flags + unit, flag_tag(epoch, kFlagAgg));
+  }
+
+  // ---------------- carry entering the stripe's end ----------------
+  float X[4][4];
+  float a_in = 1.f;
+  if (ci == 0) {
+    zero44(X);
+  } else {
+    LookbackBufs lb{p.flags, p.a_agg, p.a_inc, p.st_agg, p.st_inc, p.hdr};
+    lookback_scalar_state<4>(X, a_in, lb, ci, (uint32_t)bh, (uint32_t)BH, epoch, unit,
+                             reinterpret_cast<float*>(smem + SM_MISC + 64),
+                             reinterpret_cast<volatile uint32_t*>(smem + SM_MISC + 16));
+  }
+  if (n1 > 0) {
+    float4* dst = reinterpret_cast<float4*>(p.st_inc + st_off);
+#pragma unroll
+    for (int n = 0; n < 4; ++n)
+      __stcg(dst + n, make_float4(fmaf(A_agg, X[n][0], agg[n][0]), fmaf(A_agg, X[n][1], agg[n][1]),
+                                  fmaf(A_agg, X[n][2], agg[n][2]), fmaf(A_agg, X[n][3], agg[n][3])));
+    if (tid == 0) __stcg(p.a_inc + unit, A_agg * a_in);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) st_release_u32(p.flags + unit, flag_tag(epoch, kFlagInc));
+  }
+
+  // ---------------- pass 2: chunks in reverse ----------------
+  const int gl = c_begin + nc - 1;
+  float2 fnext = gate_load(fh, T, gl, lane);
+  for (int j = 0; j < nc; ++j) {
+    const int gc = gl - j;
+    const int slot = j % STAGES;
+    const uint8_t* base = smem + SM_RING + slot * SLOT;
+    const WGates gt = warp_gates(fnext, lane);
+    if (j + 1 < nc) fnext = gate_load(fh, T, gc - 1, lane);
+    if (warp == 0) {
+      *reinterpret_cast<float2*>(sgl + 2 * lane) = make_float2(gt.l0, gt.l1);
+      *reinterpret_cast<float2*>(sgw + 2 * lane) = make_float2(gt.w0, gt.w1);
+    }
+    if (!mbar_wait(&bars[slot], (j / STAGES) & 1)) ok = false;
+    {
+      const float e0 = fast_exp2(gt.l0), e1 = fast_exp2(gt.l1);
+      build_rows(qh_tile, base + T_Q * TILE, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+      build_rows(kw_tile, base + T_K * TILE, step_val(gt.w0, gt.w1, br0), step_val(gt.w0, gt.w1, br1),
+                 tid);
+      store_frag_bf16(x_tile, X, fr);
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    // group 1: products of the raw tiles and the carry
+    {
+      const uint32_t qb = smem_u32(base + T_Q * TILE), kb = smem_u32(base + T_K * TILE),
+                     vb = smem_u32(base + T_V * TILE), db = smem_u32(base + T_DO * TILE),
+                     sb = smem_u32(base + T_S * TILE);
+      if (warp == 0 && lane == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_M1, db, false, vb, false, false);   // dO V^T
+        umma_64x64x64(tbase + TM_PQ, qb, false, kb, false, false);   // Q K^T
+        umma_commit(bar_a);
+      } else if (warp == 1 && lane == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_DOS, db, false, sb, false, false);                // dO S_in^T
+        umma_64x64x64(tbase + TM_DX, smem_u32(qh_tile), true, db, true, false);   // Q^^T dO
+        umma_commit(bar_b);
+      } else if (warp == 2 && lane == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_VX, vb, false, smem_u32(x_tile), false, false);  // V X^T
+        umma_64x64x64(tbase + TM_KX, kb, false, smem_u32(x_tile), true, false);   // K X
+        umma_commit(bar_c);
+      } else if (warp == 3 && lane == 0) {
+        issue(n1 + j + STAGES - 1);  // into the slot of chunk j-1, released at the barrier
+      }
+      __syncwarp();
+    }
+    // per-element decays of this thread's fragment: rows u, columns s
+    const int ua = fr.r0, ub = ua + 8;
+    const float lua = sgl[ua], lub = sgl[ub];
+    float ls[4][2], ws[4][2];
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const int s0 = 8 * (4 * hf + n) + 2 * c4;
+      const float2 l2 = *reinterpret_cast<const float2*>(sgl + s0);
+      const float2 w2 = *reinterpret_cast<const float2*>(sgw + s0);
+      ls[n][0] = l2.x; ls[n][1] = l2.y;
+      ws[n][0] = w2.x; ws[n][1] = w2.y;
+    }
+    wait_bar(bar_a, ph_a);
+    tc_fence_after();
+    {
+      uint32_t r_m[16], r_p[16];
+      tmem_ld_16x32_async(r_m, tw + TM_M1);
+      tmem_ld_16x32_async(r_p, tw + TM_PQ);
+      tmem_wait_ld();
+      float m1[4][4], pq[4][4], E[4][4];
+      frag_from_u32(m1, r_m);
+      frag_from_u32(pq, r_p);
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int s = 8 * (4 * hf + n) + 2 * c4 + e;
+          const float da = s <= ua ? fast_exp2(lua - ls[n][e]) : 0.f;
+          const float db = s <= ub ? fast_exp2(lub - ls[n][e]) : 0.f;
+          m1[n][e] *= da;
+          m1[n][2 + e] *= db;
+          // E = M1d o PQ o w (one decay factor), strictly below the diagonal
+          E[n][e] = s < ua ? m1[n][e] * pq[n][e] * ws[n][e] : 0.f;
+          E[n][2 + e] = s < ub ? m1[n][2 + e] * pq[n][2 + e] * ws[n][e] : 0.f;
+          pq[n][e] *= da;
+          pq[n][2 + e] *= db;
+        }
+      store_frag_bf16(m1_tile, m1, fr);
+      store_frag_bf16(pq_tile, pq, fr);
+      // W_t = sum_{u >= t > s} E[u][s]: row-exclusive prefix F over this warp's
+      // 32 columns, then column sums of F over the rows u >= t.  The warps of
+      // the upper triangle (rows < 32 <= columns) hold no E.
+      const bool live = !(hf == 1 && qd < 2);
+      float colp[4][2];
+      if (live) {
+        float rowtot[2] = {0.f, 0.f};
+        float F[4][4];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float base_n = 0.f;
+#pragma unroll
+          for (int n = 0; n < 4; ++n) {
+            const float pr = E[n][2 * h] + E[n][2 * h + 1];
+            float inc = pr;
+            float y = __shfl_up_sync(0xffffffffu, inc, 1, 4);
+            if (c4 >= 1) inc += y;
+            y = __shfl_up_sync(0xffffffffu, inc, 2, 4);
+            if (c4 >= 2) inc += y;
+            const float tot = __shfl_sync(0xffffffffu, inc, 3, 4);
+            // exclusive value from the neighbour (not inc - pr: E[u][t] itself
+            // can exceed the terms before it by many orders of magnitude)
+            float prev = __shfl_up_sync(0xffffffffu, inc, 1, 4);
+            if (c4 == 0) prev = 0.f;
+            const float ex = base_n + prev;
+            F[n][2 * h] = ex;
+            F[n][2 * h + 1] = ex + E[n][2 * h];
+            base_n += tot;
+          }
+          rowtot[h] = base_n;
+        }
+        if (hf == 0 && c4 == 0) {
+          rowT[ua] = rowtot[0];
+          rowT[ub] = rowtot[1];
+        }
+#pragma unroll
+        for (int n = 0; n < 4; ++n)
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int s = 8 * (4 * hf + n) + 2 * c4 + e;
+            float v = (ua >= s ? F[n][e] : 0.f) + (ub >= s ? F[n][2 + e] : 0.f);
+            v += __shfl_xor_sync(0xffffffffu, v, 4);
+            v += __shfl_xor_sync(0xffffffffu, v, 8);
+            v += __shfl_xor_sync(0xffffffffu, v, 16);
+            colp[n][e] = v;
+          }
+      } else {
+#pragma unroll
+        for (int n = 0; n < 4; ++n) colp[n][0] = colp[n][1] = 0.f;
+      }
+      if (g == 0) {
+#pragma unroll
+        for (int n = 0; n < 4; ++n) {
+          const int s0 = 8 * (4 * hf + n) + 2 * c4;
+          *reinterpret_cast<float2*>(colW + qd * 64 + s0) = make_float2(colp[n][0], colp[n][1]);
+        }
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    // group 2: the masked products
+    {
+      const uint32_t qb = smem_u32(base + T_Q * TILE), db = smem_u32(base + T_DO * TILE);
+      if (warp == 0 && lane == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_DQ2, smem_u32(m1_tile), false, smem_u32(kw_tile), true, false);
+        umma_commit(bar_d);
+      } else if (warp == 1 && lane == 0) {
+        tc_fence_after();
+        umma_64x64x64(tbase + TM_DK2, smem_u32(m1_tile), true, qb, true, false);
+        umma_64x64x64(tbase + TM_DV2, smem_u32(pq_tile), true, db, true, false);
+        umma_commit(bar_e);
+      }
+      __syncwarp();
+    }
+    // carry, z and y from group 1
+    float dos[4][4], vx[4][4], kx[4][4];
+    float zp[2] = {0.f, 0.f}, yp[2] = {0.f, 0.f}, sg = 0.f;
+    const float eL = fast_exp2(gt.tot);
+    {
+      wait_bar(bar_b, ph_b);
+      wait_bar(bar_c, ph_c);
+      tc_fence_after();
+      uint32_t r_dos[16], r_dx[16], r_vx[16], r_kx[16];
+      tmem_ld_16x32_async(r_dos, tw + TM_DOS);
+      tmem_ld_16x32_async(r_dx, tw + TM_DX);
+      tmem_ld_16x32_async(r_vx, tw + TM_VX);
+      tmem_ld_16x32_async(r_kx, tw + TM_KX);
+      float sin_[4][4], qf[4][4], kf[4][4];
+      load_frag_bf16(sin_, base + T_S * TILE, fr);
+      load_frag_bf16(qf, base + T_Q * TILE, fr);
+      load_frag_bf16(kf, base + T_K * TILE, fr);
+      tmem_wait_ld();
+      float dx[4][4];
+      frag_from_u32(dos, r_dos);
+      frag_from_u32(dx, r_dx);
+      frag_from_u32(vx, r_vx);
+      frag_from_u32(kx, r_kx);
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          sg = fmaf(X[n][e], sin_[n][e], sg);
+          X[n][e] = fmaf(eL, X[n][e], dx[n][e]);
+          zp[e >> 1] = fmaf(qf[n][e], dos[n][e], zp[e >> 1]);
+          yp[e >> 1] = fmaf(kf[n][e], vx[n][e], yp[e >> 1]);
+        }
+      wait_bar(bar_d, ph_d);
+      wait_bar(bar_e, ph_e);
+      tc_fence_after();
+      uint32_t r_q2[16], r_k2[16], r_v2[16];
+      tmem_ld_16x32_async(r_q2, tw + TM_DQ2);
+      tmem_ld_16x32_async(r_k2, tw + TM_DK2);
+      tmem_ld_16x32_async(r_v2, tw + TM_DV2);
+      tmem_wait_ld();
+      float q2[4][4], k2[4][4], v2[4][4];
+      frag_from_u32(q2, r_q2);
+      frag_from_u32(k2, r_k2);
+      frag_from_u32(v2, r_v2);
+      // rows of this thread: steps ua, ub (dq rows t, dk/dv rows s)
+      const float ea = fast_exp2(lua), eb = fast_exp2(lub);
+      const float La = fast_exp2(gt.tot - lua), Lb = fast_exp2(gt.tot - lub);
+      const float wa = sgw[ua], wb = sgw[ub];
+      float kp[2] = {0.f, 0.f};
+      float o_q[4][4], o_k[4][4], o_v[4][4];
+#pragma unroll
+      for (int n = 0; n < 4; ++n)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const bool hi = e >= 2;
+          const float ex = hi ? eb : ea, Lx = hi ? Lb : La, wx = hi ? wb : wa;
+          o_q[n][e] = fmaf(ex, dos[n][e], q2[n][e]);
+          o_k[n][e] = wx * fmaf(Lx, vx[n][e], k2[n][e]);
+          o_v[n][e] = wx * fmaf(Lx, kx[n][e], v2[n][e]);
+          kp[e >> 1] = fmaf(kf[n][e], k2[n][e], kp[e >> 1]);
+        }
+      store_rows_bf16(p.dq, bh, T, gc, o_q, fr);
+      store_rows_bf16(p.dk, bh, T, gc, o_k, fr);
+      store_rows_bf16(p.dv, bh, T, gc, o_v, fr);
+      // per-row partials over this warp's 32 columns
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        zp[h] = quad_sum(zp[h]);
+        yp[h] = quad_sum(yp[h]);
+        kp[h] = quad_sum(kp[h]);
+      }
+      if (c4 == 0) {
+        rowZ[hf * 64 + ua] = zp[0];
+        rowZ[hf * 64 + ub] = zp[1];
+        rowY[hf * 64 + ua] = yp[0];
+        rowY[hf * 64 + ub] = yp[1];
+        rowK[hf * 64 + ua] = kp[0];
+        rowK[hf * 64 + ub] = kp[1];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sg += __shfl_xor_sync(0xffffffffu, sg, o);
+      if (lane == 0) sig[warp] = sg;
+    }
+    tc_fence_before();
+    __syncthreads();
+    // df of the chunk: one warp, lane l owns steps 2l and 2l+1
+    if (warp == NTHREADS / 32 - 1) {
+      const int t0 = 2 * lane;
+      float z0 = rowZ[t0] + rowZ[64 + t0], z1 = rowZ[t0 + 1] + rowZ[64 + t0 + 1];
+      float y0 = rowY[t0] + rowY[64 + t0], y1 = rowY[t0 + 1] + rowY[64 + t0 + 1];
+      const float k0 = rowK[t0] + rowK[64 + t0], k1 = rowK[t0 + 1] + rowK[64 + t0 + 1];
+      float S0sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) S0sum += sig[w];
+      const float f0 = fast_exp2(gt.x0), f1 = fast_exp2(gt.x1);
+      // R_t = z_t + f_{t+1} R_{t+1} (suffix), as affine maps over lanes
+      const float f2 = __shfl_down_sync(0xffffffffu, f0, 1);  // f of step 2l+2 (lane 31: unused)
+      float A = lane < 31 ? f1 * f2 : 0.f;
+      float B = fmaf(f1, z1, z0);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float A2 = __shfl_down_sync(0xffffffffu, A, o);
+        const float B2 = __shfl_down_sync(0xffffffffu, B, o);
+        if (lane + o < 32) {
+          B = fmaf(A, B2, B);
+          A *= A2;
+        }
+      }
+      const float Rnext = __shfl_down_sync(0xffffffffu, B, 1);  // R_{2l+2} (lane 31: none)
+      const float R0 = B;
+      const float R1 = lane < 31 ? fmaf(f2, Rnext, z1) : z1;
+      // P_t = f_t P_{t-1} + w_t y_t (prefix)
+      float PA = f0 * f1;
+      float PB = fmaf(f1 * gt.w0, y0, gt.w1 * y1);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float A2 = __shfl_up_sync(0xffffffffu, PA, o);
+        const float B2 = __shfl_up_sync(0xffffffffu, PB, o);
+        if (lane >= o) {
+          PB = fmaf(PA, B2, PB);
+          PA *= A2;
+        }
+      }
+      float Pm1 = __shfl_up_sync(0xffffffffu, PB, 1);  // P_{2l-1}
+      if (lane == 0) Pm1 = 0.f;
+      const float P0 = fmaf(f0, Pm1, gt.w0 * y0);      // P_{2l}
+      // W_t: column sums of the E prefix plus, for t >= 32, the suffix of the
+      // left half's row totals
+      float W0 = colW[t0] + colW[64 + t0] + colW[128 + t0] + colW[192 + t0];
+      float W1 = colW[t0 + 1] + colW[64 + t0 + 1] + colW[128 + t0 + 1] + colW[192 + t0 + 1];
+      {
+        const float r0 = rowT[t0], r1 = rowT[t0 + 1];
+        float sfx = r0 + r1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_down_sync(0xffffffffu, sfx, o);
+          if (lane + o < 32) sfx += y;
+        }
+        float below = __shfl_down_sync(0xffffffffu, sfx, 1);  // rows >= 2l + 2
+        if (lane == 31) below = 0.f;
+        if (t0 >= 32) {
+          W0 += sfx;
+          W1 += r1 + below;
+        }
+      }
+      const float lup = __shfl_up_sync(0xffffffffu, gt.l1, 1);
+      const float lprev0 = lane > 0 ? lup : 0.f;  // l_{2l-1}
+      const float L = gt.tot;
+      const float d0 = fast_exp2(L - gt.x0) * S0sum + fast_exp2(lprev0) * R0 +
+                       fast_exp2(L - gt.l0) * Pm1 + fast_exp2(-gt.x0) * W0 -
+                       (k0 + fast_exp2(L - gt.l0) * y0);
+      const float d1 = fast_exp2(L - gt.x1) * S0sum + fast_exp2(gt.l0) * R1 +
+                       fast_exp2(L - gt.l1) * P0 + fast_exp2(-gt.x1) * W1 -
+                       (k1 + fast_exp2(L - gt.l1) * y1);
+      const int ta = gc * CH + t0;
+      const size_t off = (size_t)bh * T + ta;
+      float* dfo = p.df + off;
+      if (ta + 1 < T && (off & 1) == 0) {
+        *reinterpret_cast<float2*>(dfo) = make_float2(d0, d1);
+      } else {
+        if (ta < T) dfo[0] = d0;
+        if (ta + 1 < T) dfo[1] = d1;
+      }
+    }
+  }
+  if (stripe == 0 && p.dS0) store_frag_rowmajor(p.dS0 + (size_t)bh * D * D, X, fr);
+  if (!ok) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, TMEM_COLS);
+  }
+  if (tid == 0) finish_cta(p.hdr, epoch, gridDim.x);
+}
+
+}  // namespace bwd
+}  // namespace gated
+}  // namespace mogt
+
+using namespace mogt;
+using namespace mogt::gated;
+
+namespace mogt {
+namespace gated {
+
+size_t bwd_tc_workspace_bytes(int64_t BH, int64_t T) {
+  const Plan pl = make_plan(BH, T, sm_count());
+  return ws_layout((size_t)BH * pl.nstripes).total;
+}
+
+// Tensor-core backward; arguments are checked by the caller.
+int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, const void* d_o,
+                  const void* chunk_states, void* dq, void* dk, void* dv, float* df, float* dS0,
+                  int BH, int T, void* workspace, size_t workspace_bytes, cudaStream_t s) {
+  const Plan pl = make_plan(BH, T, sm_count());
+  const size_t NU = (size_t)BH * pl.nstripes;
+  if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
+  const WsLayout L = ws_layout(NU);
+  if (!workspace || workspace_bytes < L.total) return MOGT_ERR_WORKSPACE;
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOGT_ERR_ALIGN;
+  CUtensorMap maps[5];
+  const void* srcs[5] = {q, k, v, d_o, chunk_states};
+  for (int i = 0; i < 5; ++i) {
+    const cuuint64_t rows = i == 4 ? (cuuint64_t)pl.nchunks * CH : (cuuint64_t)T;
+    cuuint64_t dims[3] = {(cuuint64_t)D, rows, (cuuint64_t)BH};
+    cuuint64_t strides[2] = {(cuuint64_t)D * 2, rows * D * 2};
+    cuuint32_t box[3] = {(cuuint32_t)D, (cuuint32_t)CH, 1};
+    if (mogt_host::encode_tiled(&maps[i], CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3,
+                                const_cast<void*>(srcs[i]), dims, strides, box,
+                                CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+      return MOGT_ERR_LAUNCH;
+  }
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  bwd::Params P;
+  P.f = f;
+  P.dq = static_cast<__nv_bfloat16*>(dq);
+  P.dk = static_cast<__nv_bfloat16*>(dk);
+  P.dv = static_cast<__nv_bfloat16*>(dv);
+  P.df = df;
+  P.dS0 = dS0;
+  P.hdr = reinterpret_cast<WsHeader*>(ws);
+  P.flags = reinterpret_cast<uint32_t*>(ws + L.flags);
+  P.a_agg = reinterpret_cast<float*>(ws + L.a_agg);
+  P.a_inc = reinterpret_cast<float*>(ws + L.a_inc);
+  P.st_agg = reinterpret_cast<float*>(ws + L.st_agg);
+  P.st_inc = reinterpret_cast<float*>(ws + L.st_inc);
+  P.T = T;
+  P.BH = BH;
+  P.nchunks = pl.nchunks;
+  P.cps = pl.cps;
+  P.nstripes = pl.nstripes;
+  cudaFuncSetAttribute(bwd::gated_bwd_stripe, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       bwd::SM_ALLOC);
+  bwd::gated_bwd_stripe<<<(unsigned)NU, NTHREADS, bwd::SM_ALLOC, s>>>(maps[0], maps[1], maps[2],
+                                                                      maps[3], maps[4], P);
+  return mogt_host::launch_status();
+}
+
+}  // namespace gated
+}  // namespace mogt

@@ -39,13 +39,15 @@ __device__ __forceinline__ float2 gate_load(const float* fh, int T, int gc, int 
 // 2l and 2l+1 (inclusive log2 cumulative gate l, 1 - f as w); tot is the log2
 // decay of the whole chunk (all lanes).
 struct WGates {
-  float l0, l1, w0, w1, tot;
+  float l0, l1, w0, w1, x0, x1, tot;
 };
 __device__ __forceinline__ WGates warp_gates(float2 fv, int lane) {
   WGates gt;
   const float x0 = clamped_log2(fv.x), x1 = clamped_log2(fv.y);
   gt.w0 = 1.f - fv.x;
   gt.w1 = 1.f - fv.y;
+  gt.x0 = x0;
+  gt.x1 = x1;
   const float pair = x0 + x1;
   float inc = pair;
 #pragma unroll
@@ -133,6 +135,20 @@ __device__ __forceinline__ void store_frag_rowmajor_bf16(__nv_bfloat16* dst, con
   }
 }
 
+// Inverse of store_frag_bf16: this thread's fragment of a swizzled bf16 tile.
+__device__ __forceinline__ void load_frag_bf16(float (&s)[4][4], const uint8_t* tile, Frag fr) {
+#pragma unroll
+  for (int n = 0; n < 4; ++n) {
+    const uint32_t chunk = 4 * fr.hf + n, col = 4u * fr.c4;
+    const uint32_t a = *reinterpret_cast<const uint32_t*>(tile + sw128(fr.r0, chunk) + col);
+    const uint32_t b = *reinterpret_cast<const uint32_t*>(tile + sw128(fr.r0 + 8, chunk) + col);
+    s[n][0] = __uint_as_float(a << 16);
+    s[n][1] = __uint_as_float(a & 0xFFFF0000u);
+    s[n][2] = __uint_as_float(b << 16);
+    s[n][3] = __uint_as_float(b & 0xFFFF0000u);
+  }
+}
+
 __device__ __forceinline__ void load_frag_rowmajor(float (&s)[4][4], const float* src, Frag fr) {
 #pragma unroll
   for (int n = 0; n < 4; ++n) {
@@ -141,6 +157,50 @@ __device__ __forceinline__ void load_frag_rowmajor(float (&s)[4][4], const float
     const float2 hi = __ldg(reinterpret_cast<const float2*>(src + (fr.r0 + 8) * D + j));
     s[n][0] = lo.x; s[n][1] = lo.y; s[n][2] = hi.x; s[n][3] = hi.y;
   }
+}
+
+// ---- host-side stripe planning and workspace layout (forward and backward) ----
+constexpr int MAX_CPS = 256;              // chunks per stripe (per-stripe decay tables)
+
+// Look-back workspace after the 256-byte header: per unit a flag, aggregate
+// and inclusive decays, and aggregate and inclusive 64x64 fp32 states.
+struct WsLayout {
+  size_t flags, a_agg, a_inc, st_agg, st_inc, total;
+};
+inline WsLayout ws_layout(size_t NU) {
+  WsLayout l;
+  l.flags = sizeof(WsHeader);
+  l.a_agg = l.flags + mogt_host::align_up(NU * 4, 256);
+  l.a_inc = l.a_agg + mogt_host::align_up(NU * 4, 256);
+  l.st_agg = l.a_inc + mogt_host::align_up(NU * 4, 256);
+  l.st_inc = l.st_agg + NU * D * D * 4;
+  l.total = l.st_inc + NU * D * D * 4;
+  return l;
+}
+
+// Chunks of a head cut into stripes so that BH x stripes is about one wave of
+// `resident` CTAs; a stripe holds at most MAX_CPS chunks.
+struct Plan {
+  int nchunks, cps, nstripes;
+};
+inline Plan make_plan(int64_t BH, int64_t T, int resident) {
+  Plan p;
+  p.nchunks = (int)((T + CH - 1) / CH);
+  int64_t sph = BH >= resident ? 1 : resident / BH;
+  if (sph > p.nchunks) sph = p.nchunks;
+  if (sph < 1) sph = 1;
+  const int64_t min_sph = (p.nchunks + MAX_CPS - 1) / MAX_CPS;
+  if (sph < min_sph) sph = min_sph;
+  p.cps = (int)((p.nchunks + sph - 1) / sph);
+  p.nstripes = (p.nchunks + p.cps - 1) / p.cps;
+  return p;
+}
+
+inline int sm_count() {
+  int dev = 0, nsm = 148;
+  if (cudaGetDevice(&dev) == cudaSuccess)
+    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  return nsm;
 }
 
 }  // namespace gated

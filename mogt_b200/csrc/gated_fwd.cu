@@ -65,7 +65,6 @@ namespace gated {
 constexpr int STAGES = 3;                 // pass-2 ring: q, k, v per slot
 constexpr int P1_STAGES = 5;              // pass-1 ring: k, v per slot
 constexpr int P1_AHEAD = 3;               // pass-1 chunks loading ahead
-constexpr int MAX_CPS = 256;              // chunks per stripe (suffix table)
 constexpr int SLOT = 3 * TILE;            // q, k, v of one chunk
 
 constexpr int SM_RING = 0;
@@ -105,44 +104,6 @@ struct Params {
   float* st_inc;
   int T, BH, nchunks, cps, nstripes;
 };
-
-struct WsLayout {
-  size_t flags, a_agg, a_inc, st_agg, st_inc, total;
-};
-inline WsLayout ws_layout(size_t NU) {
-  WsLayout l;
-  l.flags = sizeof(WsHeader);
-  l.a_agg = l.flags + mogt_host::align_up(NU * 4, 256);
-  l.a_inc = l.a_agg + mogt_host::align_up(NU * 4, 256);
-  l.st_agg = l.a_inc + mogt_host::align_up(NU * 4, 256);
-  l.st_inc = l.st_agg + NU * D * D * 4;
-  l.total = l.st_inc + NU * D * D * 4;
-  return l;
-}
-
-struct Plan {
-  int nchunks, cps, nstripes;
-};
-inline Plan make_plan(int64_t BH, int64_t T, int resident) {
-  Plan p;
-  p.nchunks = (int)((T + CH - 1) / CH);
-  int64_t sph = BH >= resident ? 1 : resident / BH;
-  if (sph > p.nchunks) sph = p.nchunks;
-  if (sph < 1) sph = 1;
-  // bound the stripe length (suffix-decay table)
-  const int64_t min_sph = (p.nchunks + MAX_CPS - 1) / MAX_CPS;
-  if (sph < min_sph) sph = min_sph;
-  p.cps = (int)((p.nchunks + sph - 1) / sph);
-  p.nstripes = (p.nchunks + p.cps - 1) / p.cps;
-  return p;
-}
-
-inline int resident_ctas() {
-  int dev = 0, nsm = 148;
-  if (cudaGetDevice(&dev) == cudaSuccess)
-    cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  return 2 * nsm;
-}
 
 template <bool OUT_F32>
 __global__ void __launch_bounds__(NTHREADS, 2)
@@ -615,7 +576,7 @@ size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
                                            int in_dtype) {
   if (in_dtype != MOGT_DTYPE_BF16 || dk != D || dv != D || T <= 0 || BH <= 0)
     return sizeof(WsHeader);
-  const Plan pl = make_plan(BH, T, resident_ctas());
+  const Plan pl = make_plan(BH, T, 2 * sm_count());
   return ws_layout((size_t)BH * pl.nstripes).total;
 }
 
@@ -640,7 +601,7 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
   if (!aligned16(k) || !aligned16(v) || (q && !aligned16(q)) || (o && !aligned16(o)))
     return MOGT_ERR_ALIGN;
-  const Plan pl = make_plan(BH, T, resident_ctas());
+  const Plan pl = make_plan(BH, T, 2 * sm_count());
   const size_t NU = (size_t)BH * pl.nstripes;
   if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
   const WsLayout L = ws_layout(NU);
@@ -733,7 +694,7 @@ extern "C" int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const v
   size_t clear_bytes = 0;
   if (in_dtype == MOGT_DTYPE_BF16 && dk == D && dv == D) {
     if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
-    const Plan pl = make_plan(BH, T, resident_ctas());
+    const Plan pl = make_plan(BH, T, 2 * sm_count());
     const WsLayout L = ws_layout((size_t)BH * pl.nstripes);
     if (L.total > kStaticScratchBytes) return MOGT_ERR_TOO_LARGE;
     clear_bytes = L.st_agg;  // header, flags and decays must start at zero

@@ -79,22 +79,37 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     return o, S_fin, dec, seg
 
 
-def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False):
+def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False, chunk_states=None):
     """Gradients of sum(o * do) for o = gated_scan(q, k, v, f): returns
     (dq, dk, dv, df, dS0) with dq, dk, dv in the input dtype, df fp32 and dS0
-    (gradient of the initial state) fp32 or None."""
-    _require_cuda(q, k, v, f, do, initial_state, what="gated_scan backward")
+    (gradient of the initial state) fp32 or None.
+
+    float32 inputs: exact sequential kernels (any dk, dv <= 128).
+    bfloat16 inputs (dk = dv = 64): the reverse-time chunked tensor-core
+    kernel; `chunk_states` must be the per-chunk states returned by
+    gated_scan_fwd(..., save_states=True) on the same inputs and initial state."""
+    _require_cuda(q, k, v, f, do, initial_state, chunk_states, what="gated_scan backward")
     B, H, T, dk = k.shape
     dv = v.shape[-1]
     if q.shape != k.shape or v.shape[:3] != (B, H, T) or f.shape != (B, H, T) or do.shape != v.shape:
         raise ValueError("q, k: [B, H, T, dk]; v, do: [B, H, T, dv]; f: [B, H, T]")
     dt = k.dtype
-    if dt != torch.float32:
-        raise ValueError("the gated-scan backward currently takes float32 inputs")
+    if dt not in (torch.float32, torch.bfloat16):
+        raise ValueError("the gated-scan backward takes float32 or bfloat16 inputs")
     dev = k.device
     q, k, v, do = (t.to(dt).contiguous() for t in (q, k, v, do))
     f = f.to(torch.float32).contiguous()
-    S0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    S0 = None
+    cs = None
+    if dt == torch.bfloat16:
+        nch = gated_num_chunks(T, dk, dv, dt)
+        if chunk_states is None or tuple(chunk_states.shape) != (B, H, nch, dk, dv) \
+                or chunk_states.dtype != torch.bfloat16:
+            raise ValueError("bfloat16 backward needs the forward's chunk_states "
+                             f"[B, H, {nch}, {dk}, {dv}] bfloat16")
+        cs = chunk_states.contiguous()
+    else:
+        S0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
     gq, gk = torch.empty_like(q), torch.empty_like(k)
     gv = torch.empty_like(v)
     gf = torch.empty(B, H, T, dtype=torch.float32, device=dev)
@@ -103,10 +118,13 @@ def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False):
     code = N.dtype_code(dt)
     nbytes = L.mogt_gated_scan_bwd_workspace_bytes(B * H, T, dk, dv, code)
     with torch.cuda.device(dev):
-        ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
+        if dt == torch.bfloat16:
+            ws = N.workspaces.get(dev, nbytes)
+        else:
+            ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
         st = L.mogt_gated_scan_bwd(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(do), N.ptr(S0),
-                                   N.ptr(gq), N.ptr(gk), N.ptr(gv), N.ptr(gf), N.ptr(gS0), B * H, T,
-                                   dk, dv, code, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
+                                   N.ptr(cs), N.ptr(gq), N.ptr(gk), N.ptr(gv), N.ptr(gf), N.ptr(gS0),
+                                   B * H, T, dk, dv, code, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
     N.check(st, "mogt_gated_scan_bwd")
     return gq, gk, gv, gf, gS0
 
