@@ -120,20 +120,45 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t by
                : "memory");
 }
 
-// Bounded parity wait.  Returns false on timeout.
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// Named barrier over `count` threads (a multiple of 32); id 0 is __syncthreads.
+__device__ __forceinline__ void group_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// One suspending parity probe: the thread sleeps until the phase completes or
+// about `hint_ns` have passed.
+__device__ __forceinline__ bool mbar_try_wait(uint32_t addr, uint32_t phase, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(addr), "r"(phase), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
+// Bounded parity wait: suspending probes, given up after kWaitLimitNs of
+// wall time (the caller records MOGT_ERR_TIMEOUT).  Returns false on timeout.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
   const uint32_t addr = smem_u32(bar);
-  for (uint32_t it = 0; it < kSpinLimit; ++it) {
-    uint32_t done;
-    asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-        " selp.u32 %0, 1, 0, p;\n}\n"
-        : "=r"(done)
-        : "r"(addr), "r"(phase)
-        : "memory");
-    if (done) return true;
+  if (mbar_try_wait(addr, phase, 1000000u)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait(addr, phase, 1000000u)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
   }
-  return false;
 }
 
 // 3-D tiled TMA load (no multicast) into shared memory, completion counted on
@@ -145,6 +170,26 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1), "r"(c2)
       : "memory");
+}
+
+// 3-D tiled TMA store from shared memory (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int32_t c0,
+                                             int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until at most N committed bulk groups of this thread still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+__device__ __forceinline__ void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
@@ -290,6 +335,26 @@ __device__ __forceinline__ void umma_64x64x64(uint32_t d_tmem, uint32_t a_saddr,
     umma_bf16(d_tmem, ad0 + astep * kk, bd0 + bstep * kk, idesc, accumulate || kk > 0);
 }
 
+// Two independent 64x64x64 products with their K steps interleaved, so that
+// the tensor pipe can overlap the two accumulation chains.
+__device__ __forceinline__ void umma_64x64x64_x2(uint32_t d0, uint32_t a0, bool a0_mn, uint32_t b0,
+                                                 bool b0_mn, uint32_t d1, uint32_t a1, bool a1_mn,
+                                                 uint32_t b1, bool b1_mn) {
+  const uint32_t i0 = kIdescBase | (a0_mn ? kIdescAmn : 0u) | (b0_mn ? kIdescBmn : 0u);
+  const uint32_t i1 = kIdescBase | (a1_mn ? kIdescAmn : 0u) | (b1_mn ? kIdescBmn : 0u);
+  const uint64_t ad0 = a0_mn ? umma_desc_mnmajor(a0) : umma_desc_kmajor(a0);
+  const uint64_t bd0 = b0_mn ? umma_desc_mnmajor(b0) : umma_desc_kmajor(b0);
+  const uint64_t ad1 = a1_mn ? umma_desc_mnmajor(a1) : umma_desc_kmajor(a1);
+  const uint64_t bd1 = b1_mn ? umma_desc_mnmajor(b1) : umma_desc_kmajor(b1);
+  const uint64_t as0 = a0_mn ? (2048 >> 4) : (32 >> 4), bs0 = b0_mn ? (2048 >> 4) : (32 >> 4);
+  const uint64_t as1 = a1_mn ? (2048 >> 4) : (32 >> 4), bs1 = b1_mn ? (2048 >> 4) : (32 >> 4);
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    umma_bf16(d0, ad0 + as0 * kk, bd0 + bs0 * kk, i0, kk > 0);
+    umma_bf16(d1, ad1 + as1 * kk, bd1 + bs1 * kk, i1, kk > 0);
+  }
+}
+
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))
@@ -331,6 +396,20 @@ __device__ __forceinline__ void tmem_ld_16x32_async(uint32_t (&r)[16], uint32_t 
       : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
         "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
         "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+// Warp-wide: 32 TMEM lanes (lane field of taddr = 32 * (warp % 4)) x 32
+// consecutive f32 columns; thread l gets lane 32 * (warp % 4) + l.  For an
+// M = 64 accumulator only threads 0..15 hold rows (16 * (warp % 4) + l).
+__device__ __forceinline__ void tmem_ld_32x32b_x32_async(uint32_t (&r)[32], uint32_t taddr) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,"
+      "%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+        "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+        "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
       : "r"(taddr));
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }

@@ -37,27 +37,7 @@
 #include "gated_internal.h"
 #include "lookback.cuh"
 
-#ifdef MOGT_TRACE
-// Debug-only phase timestamps (built into a separate trace library, never
-// into the product): trace[unit * 16 + k] = %globaltimer at phase k.
-__device__ unsigned long long* g_mogt_trace = nullptr;
-__device__ __forceinline__ void trace_mark(uint32_t unit, int k) {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  if (g_mogt_trace) g_mogt_trace[unit * 16 + k] = t;
-}
-#define MOGT_MARK(u, k) \
-  if (threadIdx.x == 0) trace_mark(u, k)
-// cycle-resolution marks (SM clock), for sub-phases within one CTA
-__device__ __forceinline__ void trace_clk(uint32_t unit, int k) {
-  if (g_mogt_trace) g_mogt_trace[unit * 16 + k] = clock64();
-}
-#define MOGT_CLK(u, k, cond) \
-  if (threadIdx.x == 0 && (cond)) trace_clk(u, k)
-#else
-#define MOGT_MARK(u, k)
-#define MOGT_CLK(u, k, cond)
-#endif
+#include "trace.cuh"
 
 namespace mogt {
 namespace gated {
@@ -558,13 +538,20 @@ using namespace mogt::gated;
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// The warp-specialised kernel is selectable in debug builds only, for comparison.
+static bool use_lockstep() {
+#ifdef MOGT_TRACE
+  const char* e = getenv("MOGT_FWD_WS");
+  return !(e && e[0] == '1');
+#else
+  return true;
+#endif
+}
+
 extern "C" {
 
 #ifdef MOGT_TRACE
-int mogt_debug_set_trace(void* buf) {
-  unsigned long long* p = static_cast<unsigned long long*>(buf);
-  return cudaMemcpyToSymbol(g_mogt_trace, &p, sizeof(p)) == cudaSuccess ? 0 : 4;
-}
+int mogt_debug_set_trace(void* buf) { return mogt::set_trace(buf); }
 #endif
 
 int64_t mogt_gated_scan_num_chunks(int64_t T, int64_t dk, int64_t dv, int in_dtype) {
@@ -576,8 +563,9 @@ size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
                                            int in_dtype) {
   if (in_dtype != MOGT_DTYPE_BF16 || dk != D || dv != D || T <= 0 || BH <= 0)
     return sizeof(WsHeader);
-  const Plan pl = make_plan(BH, T, 2 * sm_count());
-  return ws_layout((size_t)BH * pl.nstripes).total;
+  const size_t a = fwd_ws_workspace_bytes(BH, T);
+  const size_t b = ws_layout((size_t)BH * make_plan(BH, T, 2 * sm_count()).nstripes).total;
+  return a > b ? a : b;
 }
 
 int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
@@ -601,6 +589,9 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
   if (!aligned16(k) || !aligned16(v) || (q && !aligned16(q)) || (o && !aligned16(o)))
     return MOGT_ERR_ALIGN;
+  if (!use_lockstep())
+    return launch_fwd_ws(q, k, v, f, o, S0, S_final, decay_final, chunk_states, (int)BH, (int)T,
+                         out_dtype == MOGT_DTYPE_F32, workspace, workspace_bytes, s);
   const Plan pl = make_plan(BH, T, 2 * sm_count());
   const size_t NU = (size_t)BH * pl.nstripes;
   if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;

@@ -8,8 +8,8 @@
 // flags of up to 32 predecessors at once, finds the nearest inclusive one,
 // and all threads then accumulate the aggregates in between with pipelined
 // L2 loads.  States use the producer's fragment-native layout: thread `tid`
-// owns floats [tid*4*NF, (tid+1)*4*NF) of every 4096-float state, so
-// NF * 4 * blockDim.x == 4096.
+// of the NTH participating threads owns floats [tid*4*NF, (tid+1)*4*NF) of
+// every 4096-float state, so NF * 4 * NTH == 4096.
 #pragma once
 
 #include "common.cuh"
@@ -26,14 +26,19 @@ struct LookbackBufs {
 };
 
 // scl: 32 floats of shared memory; ctl: 4 words of shared memory.
-// Must be called by all threads of the CTA.
-template <int NF>
+// Called by the NTH threads of a warp-aligned group, `tid` = index in the
+// group, synchronised by named barrier `bar_id` (0 with NTH = blockDim.x is
+// the CTA barrier).
+template <int NF, int NTH = 256>
 __device__ __forceinline__ void lookback_scalar_state(float (&acc)[NF][4], float& a_in,
                                                       const LookbackBufs& lb, int s_self,
                                                       uint32_t base, uint32_t stride,
                                                       uint32_t epoch, uint32_t unit_id, float* scl,
-                                                      volatile uint32_t* ctl) {
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+                                                      volatile uint32_t* ctl, int tid = -1,
+                                                      int bar_id = 0) {
+  static_assert(NF * 4 * NTH == 4096, "state layout");
+  if (tid < 0) tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
 #pragma unroll
   for (int n = 0; n < NF; ++n)
 #pragma unroll
@@ -94,7 +99,7 @@ __device__ __forceinline__ void lookback_scalar_state(float (&acc)[NF][4], float
         ctl[2] = __float_as_uint(run * tot);
       }
     }
-    __syncthreads();
+    group_sync(bar_id, NTH);
     const int n = (int)ctl[0];
     const bool end = ctl[1] != 0;
     const float run_next = __uint_as_float(ctl[2]);
@@ -120,7 +125,7 @@ __device__ __forceinline__ void lookback_scalar_state(float (&acc)[NF][4], float
     }
     run = run_next;
     sp -= n;
-    __syncthreads();
+    group_sync(bar_id, NTH);
   }
 }
 
