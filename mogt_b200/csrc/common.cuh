@@ -335,26 +335,6 @@ __device__ __forceinline__ void umma_64x64x64(uint32_t d_tmem, uint32_t a_saddr,
     umma_bf16(d_tmem, ad0 + astep * kk, bd0 + bstep * kk, idesc, accumulate || kk > 0);
 }
 
-// Two independent 64x64x64 products with their K steps interleaved, so that
-// the tensor pipe can overlap the two accumulation chains.
-__device__ __forceinline__ void umma_64x64x64_x2(uint32_t d0, uint32_t a0, bool a0_mn, uint32_t b0,
-                                                 bool b0_mn, uint32_t d1, uint32_t a1, bool a1_mn,
-                                                 uint32_t b1, bool b1_mn) {
-  const uint32_t i0 = kIdescBase | (a0_mn ? kIdescAmn : 0u) | (b0_mn ? kIdescBmn : 0u);
-  const uint32_t i1 = kIdescBase | (a1_mn ? kIdescAmn : 0u) | (b1_mn ? kIdescBmn : 0u);
-  const uint64_t ad0 = a0_mn ? umma_desc_mnmajor(a0) : umma_desc_kmajor(a0);
-  const uint64_t bd0 = b0_mn ? umma_desc_mnmajor(b0) : umma_desc_kmajor(b0);
-  const uint64_t ad1 = a1_mn ? umma_desc_mnmajor(a1) : umma_desc_kmajor(a1);
-  const uint64_t bd1 = b1_mn ? umma_desc_mnmajor(b1) : umma_desc_kmajor(b1);
-  const uint64_t as0 = a0_mn ? (2048 >> 4) : (32 >> 4), bs0 = b0_mn ? (2048 >> 4) : (32 >> 4);
-  const uint64_t as1 = a1_mn ? (2048 >> 4) : (32 >> 4), bs1 = b1_mn ? (2048 >> 4) : (32 >> 4);
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    umma_bf16(d0, ad0 + as0 * kk, bd0 + bs0 * kk, i0, kk > 0);
-    umma_bf16(d1, ad1 + as1 * kk, bd1 + bs1 * kk, i1, kk > 0);
-  }
-}
-
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
                    smem_u32(bar))

@@ -538,15 +538,7 @@ using namespace mogt::gated;
 
 static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// The warp-specialised kernel is selectable in debug builds only, for comparison.
-static bool use_lockstep() {
-#ifdef MOGT_TRACE
-  const char* e = getenv("MOGT_FWD_WS");
-  return !(e && e[0] == '1');
-#else
-  return true;
-#endif
-}
+
 
 extern "C" {
 
@@ -563,9 +555,7 @@ size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
                                            int in_dtype) {
   if (in_dtype != MOGT_DTYPE_BF16 || dk != D || dv != D || T <= 0 || BH <= 0)
     return sizeof(WsHeader);
-  const size_t a = fwd_ws_workspace_bytes(BH, T);
-  const size_t b = ws_layout((size_t)BH * make_plan(BH, T, 2 * sm_count()).nstripes).total;
-  return a > b ? a : b;
+  return ws_layout((size_t)BH * make_plan(BH, T, 2 * sm_count()).nstripes).total;
 }
 
 int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
@@ -589,9 +579,6 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
   if (!aligned16(k) || !aligned16(v) || (q && !aligned16(q)) || (o && !aligned16(o)))
     return MOGT_ERR_ALIGN;
-  if (!use_lockstep())
-    return launch_fwd_ws(q, k, v, f, o, S0, S_final, decay_final, chunk_states, (int)BH, (int)T,
-                         out_dtype == MOGT_DTYPE_F32, workspace, workspace_bytes, s);
   const Plan pl = make_plan(BH, T, 2 * sm_count());
   const size_t NU = (size_t)BH * pl.nstripes;
   if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
