@@ -335,10 +335,14 @@ def run_b200(args):
     extra = {}
     if not args.no_extra:
         bb = extra_backbone(dev, world, rank)
+        sp = extra_sp(dev, world, rank) if world > 1 else None
         if rank == 0:
             extra = extra_affine(dev)
             extra["backbone"] = bb
+            extra["gated_bwd_config2"] = extra_backward(dev, B, H, T)
             extra["matrix_scan_config3"] = extra_matrix(dev)
+            if sp is not None:
+                extra["sequence_parallel_config5"] = sp
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -404,6 +408,68 @@ def extra_affine(dev):
     return {"affine_r16_c48_L32768": {"ms": ms, "GBps": alg / (ms / 1e3) / 1e9,
                                       "reference_L4_triton_hybrid_ms": 5.48,
                                       "note": "not L2-flushed (235 MB working set > L2)"}}
+
+
+def extra_backward(dev, B, H, T):
+    """BASELINE config 2, backward: the reverse-time chunked tensor-core
+    kernel on the forward's bf16 chunk states (two input sets alternated,
+    each > L2).  Algorithmic bytes per (token, head): q, k, v, do read
+    (4 x 128) + f (4) + chunk state (8192 / 64 = 128) + dq, dk, dv written
+    (3 x 128) + df (4) = 1032."""
+    import torch
+    from mogt_b200 import ops
+    sets = []
+    for seed in (3000, 4000):
+        q, k, v, f = (t.to(dev) for t in make_inputs(B, H, T, seed))
+        g = torch.randn(B, H, T, 64, generator=torch.Generator().manual_seed(seed)).to(dev).bfloat16()
+        _, _, _, cs = ops.gated_scan_fwd(q, k, v, f, save_states=True)
+        sets.append((q, k, v, f, g, cs))
+    step = lambda i: ops.gated_scan_bwd(*sets[i & 1][:5], chunk_states=sets[i & 1][5])
+    for i in range(4):
+        step(i)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 20
+    e0.record()
+    for i in range(n):
+        step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    alg = 1032 * B * H * T
+    return {"ms": ms, "tokens_per_s": B * T / (ms / 1e3), "GBps": alg / (ms / 1e3) / 1e9,
+            "algorithmic_bytes": alg, "dtype": "bf16 inputs, fp32 state/accumulate",
+            "note": "includes the Python-side output allocation; forward with saved chunk states not timed"}
+
+
+def extra_sp(dev, world, rank):
+    """one sequence of T = 262144 (B=1, H=12, 64x64) split
+    into contiguous segments over the ranks; segment carries all-gathered over
+    NCCL, local correction scan.  Time = max over ranks; whole-job tokens/s."""
+    import torch
+    import torch.distributed as dist
+    from mogt_b200.sp import gated_scan_sp
+    T = 262144
+    T_loc = T // world
+    q, k, v, f = (t.to(dev) for t in make_inputs(1, 12, T_loc, 5000 + rank))
+    run = lambda: gated_scan_sp(q, k, v, f)
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n = 10
+    e0.record()
+    for _ in range(n):
+        run()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / n
+    t = torch.tensor([ms], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    return {"ms": ms, "tokens_per_s": T / (ms / 1e3), "T": T, "ranks": world,
+            "note": "state-only segment scan + NCCL all-gather of (decay, state) carries + local scan"}
 
 
 def extra_matrix(dev):
