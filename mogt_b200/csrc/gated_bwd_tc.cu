@@ -57,7 +57,8 @@ constexpr int SM_KW = SM_QH + TILE;                // diag(w) K, [s][i]
 constexpr int SM_X = SM_KW + TILE;                 // bf16 carry X, [i][j]
 constexpr int SM_M1 = SM_X + TILE;                 // M1d, [u][s]
 constexpr int SM_PQ = SM_M1 + TILE;                // PQd, [u][s]
-constexpr int SM_GL = SM_PQ + TILE;                // l_t of the chunk [64]
+constexpr int SM_OUT = SM_PQ + TILE;               // dq, dk, dv staging tiles [3] (TMA stores)
+constexpr int SM_GL = SM_OUT + 3 * TILE;           // l_t of the chunk [64]
 constexpr int SM_GW = SM_GL + 256;                 // w_t [64]
 constexpr int SM_LPRE = SM_GW + 256;               // pass-1 prefix decays [MAX_CPS]
 constexpr int SM_ROWZ = SM_LPRE + MAX_CPS * 4;     // [2][64] halves of z_u
@@ -112,24 +113,12 @@ __device__ __forceinline__ float quad_sum(float x) {
   return x;
 }
 
-// dst (bf16, row-major [T][64]) rows of chunk gc from a fragment, rows >= T skipped
-__device__ __forceinline__ void store_rows_bf16(__nv_bfloat16* dst, int bh, int T, int gc,
-                                                const float (&s)[4][4], Frag fr) {
-  uint32_t* d32 = reinterpret_cast<uint32_t*>(dst);
-  const int ta = gc * CH + fr.r0, tb = ta + 8;
-  const size_t rowa = ((size_t)bh * T + ta) * D, rowb = ((size_t)bh * T + tb) * D;
-#pragma unroll
-  for (int n = 0; n < 4; ++n) {
-    const int j = 8 * (4 * fr.hf + n) + 2 * fr.c4;
-    if (ta < T) __stcs(d32 + (rowa + j) / 2, pack_bf16(s[n][0], s[n][1]));
-    if (tb < T) __stcs(d32 + (rowb + j) / 2, pack_bf16(s[n][2], s[n][3]));
-  }
-}
-
 __global__ void __launch_bounds__(NTHREADS, 1)
     gated_bwd_stripe(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
-                     const __grid_constant__ CUtensorMap ts, const Params p) {
+                     const __grid_constant__ CUtensorMap ts, const __grid_constant__ CUtensorMap tdq,
+                     const __grid_constant__ CUtensorMap tdk, const __grid_constant__ CUtensorMap tdv,
+                     const Params p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~uintptr_t(1023));
@@ -364,6 +353,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     }
     fence_proxy_async();
     tc_fence_before();
+    if (tid == 0) bulk_wait_read<0>();   // the previous chunk's dq, dk, dv stores have read their tiles
     __syncthreads();
     MOGT_CLK(unit, 7, j == 5);
     // group 1: products of the raw tiles and the carry
@@ -572,9 +562,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           o_v[n][e] = wx * fmaf(Lx, kx[n][e], v2[n][e]);
           kp[e >> 1] = fmaf(kf[n][e], k2[n][e], kp[e >> 1]);
         }
-      store_rows_bf16(p.dq, bh, T, gc, o_q, fr);
-      store_rows_bf16(p.dk, bh, T, gc, o_k, fr);
-      store_rows_bf16(p.dv, bh, T, gc, o_v, fr);
+      // staged in shared memory; one TMA store per matrix after the barrier
+      // (rows past T are clipped by the tensor map)
+      store_frag_bf16(smem + SM_OUT, o_q, fr);
+      store_frag_bf16(smem + SM_OUT + TILE, o_k, fr);
+      store_frag_bf16(smem + SM_OUT + 2 * TILE, o_v, fr);
+      fence_proxy_async();
       // per-row partials over this warp's 32 columns
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
@@ -597,6 +590,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     MOGT_CLK(unit, 13, j == 5);
     tc_fence_before();
     __syncthreads();
+    if (tid == 0) {
+      tma_store_3d(&tdq, smem + SM_OUT, 0, gc * CH, bh);
+      tma_store_3d(&tdk, smem + SM_OUT + TILE, 0, gc * CH, bh);
+      tma_store_3d(&tdv, smem + SM_OUT + 2 * TILE, 0, gc * CH, bh);
+      bulk_commit();
+    }
     MOGT_CLK(unit, 14, j == 5);
     // df of the chunk: one warp, lane l owns steps 2l and 2l+1
     if (warp == NTHREADS / 32 - 1) {
@@ -681,6 +680,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   }
   MOGT_MARK(unit, 4);
   if (stripe == 0 && p.dS0) store_frag_rowmajor(p.dS0 + (size_t)bh * D * D, X, fr);
+  if (tid == 0) bulk_wait<0>();
   if (!ok) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
   tc_fence_before();
   __syncthreads();
@@ -720,9 +720,9 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   const WsLayout L = ws_layout(NU);
   if (!workspace || workspace_bytes < L.total) return MOGT_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOGT_ERR_ALIGN;
-  CUtensorMap maps[5];
-  const void* srcs[5] = {q, k, v, d_o, chunk_states};
-  for (int i = 0; i < 5; ++i) {
+  CUtensorMap maps[8];
+  const void* srcs[8] = {q, k, v, d_o, chunk_states, dq, dk, dv};
+  for (int i = 0; i < 8; ++i) {
     const cuuint64_t rows = i == 4 ? (cuuint64_t)pl.nchunks * CH : (cuuint64_t)T;
     cuuint64_t dims[3] = {(cuuint64_t)D, rows, (cuuint64_t)BH};
     cuuint64_t strides[2] = {(cuuint64_t)D * 2, rows * D * 2};
@@ -753,8 +753,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   P.nstripes = pl.nstripes;
   cudaFuncSetAttribute(bwd::gated_bwd_stripe, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        bwd::SM_ALLOC);
-  bwd::gated_bwd_stripe<<<(unsigned)NU, NTHREADS, bwd::SM_ALLOC, s>>>(maps[0], maps[1], maps[2],
-                                                                      maps[3], maps[4], P);
+  bwd::gated_bwd_stripe<<<(unsigned)NU, NTHREADS, bwd::SM_ALLOC, s>>>(
+      maps[0], maps[1], maps[2], maps[3], maps[4], maps[5], maps[6], maps[7], P);
   return mogt_host::launch_status();
 }
 
