@@ -61,13 +61,16 @@ constexpr int SM_OUT = SM_PQ + TILE;               // dq, dk, dv staging tiles [
 constexpr int SM_GL = SM_OUT + 3 * TILE;           // l_t of the chunk [64]
 constexpr int SM_GW = SM_GL + 256;                 // w_t [64]
 constexpr int SM_LPRE = SM_GW + 256;               // pass-1 prefix decays [MAX_CPS]
+// per-chunk partial sums for df, double-buffered by chunk parity (df of chunk
+// j is formed during chunk j+1)
+constexpr int PART = 512 * 3 + 1024 + 256 + 64;    // one parity's partials
 constexpr int SM_ROWZ = SM_LPRE + MAX_CPS * 4;     // [2][64] halves of z_u
 constexpr int SM_ROWY = SM_ROWZ + 512;             // [2][64] halves of y_s
 constexpr int SM_ROWK = SM_ROWY + 512;             // [2][64] halves of k.(M1d^T Q)
 constexpr int SM_COLW = SM_ROWK + 512;             // [4][64] column sums of the E prefix
 constexpr int SM_ROWT = SM_COLW + 1024;            // [64] row totals of E, columns 0..31
 constexpr int SM_SIG = SM_ROWT + 256;              // [8] <X, S_in> per warp
-constexpr int SM_MISC = SM_SIG + 64;               // ticket, look-back scratch
+constexpr int SM_MISC = SM_ROWZ + 2 * PART;        // ticket, look-back scratch
 constexpr int NBARS = STAGES + P1_STAGES + 2 + 5;
 constexpr int SM_BAR = SM_MISC + 256;
 constexpr int SM_TSLOT = SM_BAR + 8 * NBARS;
@@ -129,12 +132,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   float* sgl = reinterpret_cast<float*>(smem + SM_GL);
   float* sgw = reinterpret_cast<float*>(smem + SM_GW);
   float* lpre = reinterpret_cast<float*>(smem + SM_LPRE);
-  float* rowZ = reinterpret_cast<float*>(smem + SM_ROWZ);
-  float* rowY = reinterpret_cast<float*>(smem + SM_ROWY);
-  float* rowK = reinterpret_cast<float*>(smem + SM_ROWK);
-  float* colW = reinterpret_cast<float*>(smem + SM_COLW);
-  float* rowT = reinterpret_cast<float*>(smem + SM_ROWT);
-  float* sig = reinterpret_cast<float*>(smem + SM_SIG);
+  auto part = [&](int off, int par) { return reinterpret_cast<float*>(smem + off + par * PART); };
   volatile uint32_t* bc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
   uint64_t* bars1 = bars + STAGES;
@@ -329,8 +327,95 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 
   MOGT_MARK(unit, 3);
   // ---------------- pass 2: chunks in reverse ----------------
+  // df of chunk gc from the partials of parity par: one warp, lane l owns
+  // steps 2l and 2l+1
+  auto compute_df = [&](int gc, const WGates& gt, int par) {
+    const float* rowZ = part(SM_ROWZ, par);
+    const float* rowY = part(SM_ROWY, par);
+    const float* rowK = part(SM_ROWK, par);
+    const float* colW = part(SM_COLW, par);
+    const float* rowT = part(SM_ROWT, par);
+    const float* sig = part(SM_SIG, par);
+      const int t0 = 2 * lane;
+      float z0 = rowZ[t0] + rowZ[64 + t0], z1 = rowZ[t0 + 1] + rowZ[64 + t0 + 1];
+      float y0 = rowY[t0] + rowY[64 + t0], y1 = rowY[t0 + 1] + rowY[64 + t0 + 1];
+      const float k0 = rowK[t0] + rowK[64 + t0], k1 = rowK[t0 + 1] + rowK[64 + t0 + 1];
+      float S0sum = 0.f;
+#pragma unroll
+      for (int w = 0; w < 8; ++w) S0sum += sig[w];
+      const float f0 = fast_exp2(gt.x0), f1 = fast_exp2(gt.x1);
+      // R_t = z_t + f_{t+1} R_{t+1} (suffix), as affine maps over lanes
+      const float f2 = __shfl_down_sync(0xffffffffu, f0, 1);  // f of step 2l+2 (lane 31: unused)
+      float A = lane < 31 ? f1 * f2 : 0.f;
+      float B = fmaf(f1, z1, z0);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float A2 = __shfl_down_sync(0xffffffffu, A, o);
+        const float B2 = __shfl_down_sync(0xffffffffu, B, o);
+        if (lane + o < 32) {
+          B = fmaf(A, B2, B);
+          A *= A2;
+        }
+      }
+      const float Rnext = __shfl_down_sync(0xffffffffu, B, 1);  // R_{2l+2} (lane 31: none)
+      const float R0 = B;
+      const float R1 = lane < 31 ? fmaf(f2, Rnext, z1) : z1;
+      // P_t = f_t P_{t-1} + w_t y_t (prefix)
+      float PA = f0 * f1;
+      float PB = fmaf(f1 * gt.w0, y0, gt.w1 * y1);
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const float A2 = __shfl_up_sync(0xffffffffu, PA, o);
+        const float B2 = __shfl_up_sync(0xffffffffu, PB, o);
+        if (lane >= o) {
+          PB = fmaf(PA, B2, PB);
+          PA *= A2;
+        }
+      }
+      float Pm1 = __shfl_up_sync(0xffffffffu, PB, 1);  // P_{2l-1}
+      if (lane == 0) Pm1 = 0.f;
+      const float P0 = fmaf(f0, Pm1, gt.w0 * y0);      // P_{2l}
+      // W_t: column sums of the E prefix plus, for t >= 32, the suffix of the
+      // left half's row totals
+      float W0 = colW[t0] + colW[64 + t0] + colW[128 + t0] + colW[192 + t0];
+      float W1 = colW[t0 + 1] + colW[64 + t0 + 1] + colW[128 + t0 + 1] + colW[192 + t0 + 1];
+      {
+        const float r0 = rowT[t0], r1 = rowT[t0 + 1];
+        float sfx = r0 + r1;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_down_sync(0xffffffffu, sfx, o);
+          if (lane + o < 32) sfx += y;
+        }
+        float below = __shfl_down_sync(0xffffffffu, sfx, 1);  // rows >= 2l + 2
+        if (lane == 31) below = 0.f;
+        if (t0 >= 32) {
+          W0 += sfx;
+          W1 += r1 + below;
+        }
+      }
+      const float lup = __shfl_up_sync(0xffffffffu, gt.l1, 1);
+      const float lprev0 = lane > 0 ? lup : 0.f;  // l_{2l-1}
+      const float L = gt.tot;
+      const float d0 = fast_exp2(L - gt.x0) * S0sum + fast_exp2(lprev0) * R0 +
+                       fast_exp2(L - gt.l0) * Pm1 + fast_exp2(-gt.x0) * W0 -
+                       (k0 + fast_exp2(L - gt.l0) * y0);
+      const float d1 = fast_exp2(L - gt.x1) * S0sum + fast_exp2(gt.l0) * R1 +
+                       fast_exp2(L - gt.l1) * P0 + fast_exp2(-gt.x1) * W1 -
+                       (k1 + fast_exp2(L - gt.l1) * y1);
+      const int ta = gc * CH + t0;
+      const size_t off = (size_t)bh * T + ta;
+      float* dfo = p.df + off;
+      if (ta + 1 < T && (off & 1) == 0) {
+        *reinterpret_cast<float2*>(dfo) = make_float2(d0, d1);
+      } else {
+        if (ta < T) dfo[0] = d0;
+        if (ta + 1 < T) dfo[1] = d1;
+      }
+  };
   const int gl = c_begin + nc - 1;
   float2 fnext = gate_load(fh, T, gl, lane);
+  WGates gprev{};
   for (int j = 0; j < nc; ++j) {
     const int gc = gl - j;
     const int slot = j % STAGES;
@@ -381,6 +466,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
       __syncwarp();
     }
+    // the last warp forms df of the previous chunk while the MMAs run
+    if (warp == NTHREADS / 32 - 1 && j > 0) compute_df(gc + 1, gprev, (j - 1) & 1);
     // per-element decays of this thread's fragment: rows u, columns s
     const int ua = fr.r0, ub = ua + 8;
     const float lua = sgl[ua], lub = sgl[ub];
@@ -453,8 +540,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
           rowtot[h] = base_n;
         }
         if (hf == 0 && c4 == 0) {
-          rowT[ua] = rowtot[0];
-          rowT[ub] = rowtot[1];
+          part(SM_ROWT, j & 1)[ua] = rowtot[0];
+          part(SM_ROWT, j & 1)[ub] = rowtot[1];
         }
 #pragma unroll
         for (int n = 0; n < 4; ++n)
@@ -475,7 +562,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 #pragma unroll
         for (int n = 0; n < 4; ++n) {
           const int s0 = 8 * (4 * hf + n) + 2 * c4;
-          *reinterpret_cast<float2*>(colW + qd * 64 + s0) = make_float2(colp[n][0], colp[n][1]);
+          *reinterpret_cast<float2*>(part(SM_COLW, j & 1) + qd * 64 + s0) = make_float2(colp[n][0], colp[n][1]);
         }
       }
     }
@@ -576,6 +663,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         kp[h] = quad_sum(kp[h]);
       }
       if (c4 == 0) {
+        float* rowZ = part(SM_ROWZ, j & 1);
+        float* rowY = part(SM_ROWY, j & 1);
+        float* rowK = part(SM_ROWK, j & 1);
         rowZ[hf * 64 + ua] = zp[0];
         rowZ[hf * 64 + ub] = zp[1];
         rowY[hf * 64 + ua] = yp[0];
@@ -585,7 +675,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1) sg += __shfl_xor_sync(0xffffffffu, sg, o);
-      if (lane == 0) sig[warp] = sg;
+      if (lane == 0) part(SM_SIG, j & 1)[warp] = sg;
     }
     MOGT_CLK(unit, 13, j == 5);
     tc_fence_before();
@@ -597,87 +687,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       bulk_commit();
     }
     MOGT_CLK(unit, 14, j == 5);
-    // df of the chunk: one warp, lane l owns steps 2l and 2l+1
-    if (warp == NTHREADS / 32 - 1) {
-      const int t0 = 2 * lane;
-      float z0 = rowZ[t0] + rowZ[64 + t0], z1 = rowZ[t0 + 1] + rowZ[64 + t0 + 1];
-      float y0 = rowY[t0] + rowY[64 + t0], y1 = rowY[t0 + 1] + rowY[64 + t0 + 1];
-      const float k0 = rowK[t0] + rowK[64 + t0], k1 = rowK[t0 + 1] + rowK[64 + t0 + 1];
-      float S0sum = 0.f;
-#pragma unroll
-      for (int w = 0; w < 8; ++w) S0sum += sig[w];
-      const float f0 = fast_exp2(gt.x0), f1 = fast_exp2(gt.x1);
-      // R_t = z_t + f_{t+1} R_{t+1} (suffix), as affine maps over lanes
-      const float f2 = __shfl_down_sync(0xffffffffu, f0, 1);  // f of step 2l+2 (lane 31: unused)
-      float A = lane < 31 ? f1 * f2 : 0.f;
-      float B = fmaf(f1, z1, z0);
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float A2 = __shfl_down_sync(0xffffffffu, A, o);
-        const float B2 = __shfl_down_sync(0xffffffffu, B, o);
-        if (lane + o < 32) {
-          B = fmaf(A, B2, B);
-          A *= A2;
-        }
-      }
-      const float Rnext = __shfl_down_sync(0xffffffffu, B, 1);  // R_{2l+2} (lane 31: none)
-      const float R0 = B;
-      const float R1 = lane < 31 ? fmaf(f2, Rnext, z1) : z1;
-      // P_t = f_t P_{t-1} + w_t y_t (prefix)
-      float PA = f0 * f1;
-      float PB = fmaf(f1 * gt.w0, y0, gt.w1 * y1);
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float A2 = __shfl_up_sync(0xffffffffu, PA, o);
-        const float B2 = __shfl_up_sync(0xffffffffu, PB, o);
-        if (lane >= o) {
-          PB = fmaf(PA, B2, PB);
-          PA *= A2;
-        }
-      }
-      float Pm1 = __shfl_up_sync(0xffffffffu, PB, 1);  // P_{2l-1}
-      if (lane == 0) Pm1 = 0.f;
-      const float P0 = fmaf(f0, Pm1, gt.w0 * y0);      // P_{2l}
-      // W_t: column sums of the E prefix plus, for t >= 32, the suffix of the
-      // left half's row totals
-      float W0 = colW[t0] + colW[64 + t0] + colW[128 + t0] + colW[192 + t0];
-      float W1 = colW[t0 + 1] + colW[64 + t0 + 1] + colW[128 + t0 + 1] + colW[192 + t0 + 1];
-      {
-        const float r0 = rowT[t0], r1 = rowT[t0 + 1];
-        float sfx = r0 + r1;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y = __shfl_down_sync(0xffffffffu, sfx, o);
-          if (lane + o < 32) sfx += y;
-        }
-        float below = __shfl_down_sync(0xffffffffu, sfx, 1);  // rows >= 2l + 2
-        if (lane == 31) below = 0.f;
-        if (t0 >= 32) {
-          W0 += sfx;
-          W1 += r1 + below;
-        }
-      }
-      const float lup = __shfl_up_sync(0xffffffffu, gt.l1, 1);
-      const float lprev0 = lane > 0 ? lup : 0.f;  // l_{2l-1}
-      const float L = gt.tot;
-      const float d0 = fast_exp2(L - gt.x0) * S0sum + fast_exp2(lprev0) * R0 +
-                       fast_exp2(L - gt.l0) * Pm1 + fast_exp2(-gt.x0) * W0 -
-                       (k0 + fast_exp2(L - gt.l0) * y0);
-      const float d1 = fast_exp2(L - gt.x1) * S0sum + fast_exp2(gt.l0) * R1 +
-                       fast_exp2(L - gt.l1) * P0 + fast_exp2(-gt.x1) * W1 -
-                       (k1 + fast_exp2(L - gt.l1) * y1);
-      const int ta = gc * CH + t0;
-      const size_t off = (size_t)bh * T + ta;
-      float* dfo = p.df + off;
-      if (ta + 1 < T && (off & 1) == 0) {
-        *reinterpret_cast<float2*>(dfo) = make_float2(d0, d1);
-      } else {
-        if (ta < T) dfo[0] = d0;
-        if (ta + 1 < T) dfo[1] = d1;
-      }
-      MOGT_CLK_T(unit, 15, j == 5, NTHREADS - 32);
-    }
+    gprev = gt;
   }
+  if (warp == NTHREADS / 32 - 1 && nc > 0) compute_df(c_begin, gprev, (nc - 1) & 1);
   MOGT_MARK(unit, 4);
   if (stripe == 0 && p.dS0) store_frag_rowmajor(p.dS0 + (size_t)bh * D * D, X, fr);
   if (tid == 0) bulk_wait<0>();
