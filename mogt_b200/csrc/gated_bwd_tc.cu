@@ -47,7 +47,7 @@ namespace bwd {
 
 constexpr int STAGES = 3;                  // pass-2 ring: q, k, v, do, S_in per slot
 constexpr int P1_STAGES = 7;               // pass-1 ring: q, do per slot
-constexpr int P1_AHEAD = 5;
+constexpr int P1_AHEAD = 3;                // chunks c+3, c+4 load into the slots of pair c/2 - 2
 constexpr int SLOT = 5 * TILE;
 constexpr int T_Q = 0, T_K = 1, T_V = 2, T_DO = 3, T_S = 4;
 
@@ -251,34 +251,55 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       }
     }
     __syncthreads();
-    float2 fnext = gate_load(fh, T, c_begin, lane);
-    for (int c = 0; c < n1; ++c) {
-      const WGates gt = warp_gates(fnext, lane);
-      if (c + 1 < n1) fnext = gate_load(fh, T, c_begin + c + 1, lane);
-      if (c >= 2) {
-        uint32_t ph = ((c - 2) >> 1) & 1;
-        if (!mbar_wait(&bar_k[c & 1], ph)) ok = false;
+    // chunks in pairs: two scaled tiles per CTA barrier, the pair's MMAs
+    // committed together; tile sets alternate between pairs
+    const int np = (n1 + 1) / 2;
+    float2 fa = gate_load(fh, T, c_begin, lane);
+    float2 fb = n1 > 1 ? gate_load(fh, T, c_begin + 1, lane) : make_float2(1.f, 1.f);
+    for (int pi = 0; pi < np; ++pi) {
+      const int c = 2 * pi;
+      const bool two = c + 1 < n1;
+      const WGates ga = warp_gates(fa, lane), gb = warp_gates(fb, lane);
+      if (c + 2 < n1) fa = gate_load(fh, T, c_begin + c + 2, lane);
+      if (c + 3 < n1) fb = gate_load(fh, T, c_begin + c + 3, lane);
+      if (pi >= 2) {
+        const uint32_t ph = ((pi - 2) >> 1) & 1;
+        if (!mbar_wait(&bar_k[pi & 1], ph)) ok = false;   // MMAs of pair pi-2 done
       }
-      if (tid == 0 && c + P1_AHEAD < n1) issue(c + P1_AHEAD);
+      if (tid == 0) {   // into the slots of pair pi-2
+        if (c + P1_AHEAD < n1) issue(c + P1_AHEAD);
+        if (c + 1 + P1_AHEAD < n1) issue(c + 1 + P1_AHEAD);
+      }
+      uint8_t* t0 = (pi & 1) ? x_tile : qh_tile;
+      uint8_t* t1 = (pi & 1) ? m1_tile : kw_tile;
+      uint8_t* base0 = smem + SM_RING + (c % P1_STAGES) * 2 * TILE;
+      uint8_t* base1 = smem + SM_RING + ((c + 1) % P1_STAGES) * 2 * TILE;
       if (!mbar_wait(&bars1[c % P1_STAGES], (c / P1_STAGES) & 1)) ok = false;
-      const float sc = lpre[c];
-      const float e0 = fast_exp2(sc + gt.l0), e1 = fast_exp2(sc + gt.l1);
-      uint8_t* base = smem + SM_RING + (c % P1_STAGES) * 2 * TILE;
-      uint8_t* qt = (c & 1) ? kw_tile : qh_tile;
-      build_rows(qt, base, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+      {
+        const float sc = lpre[c];
+        const float e0 = fast_exp2(sc + ga.l0), e1 = fast_exp2(sc + ga.l1);
+        build_rows(t0, base0, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+      }
+      if (two) {
+        if (!mbar_wait(&bars1[(c + 1) % P1_STAGES], ((c + 1) / P1_STAGES) & 1)) ok = false;
+        const float sc = lpre[c + 1];
+        const float e0 = fast_exp2(sc + gb.l0), e1 = fast_exp2(sc + gb.l1);
+        build_rows(t1, base1, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+      }
       fence_proxy_async();
       tc_fence_before();
       __syncthreads();
       if (tid == 0) {
         tc_fence_after();
-        umma_64x64x64(tbase + TM_AGG, smem_u32(qt), true, smem_u32(base + TILE), true, c > 0);
-        umma_commit(&bar_k[c & 1]);
+        umma_64x64x64(tbase + TM_AGG, smem_u32(t0), true, smem_u32(base0 + TILE), true, c > 0);
+        if (two) umma_64x64x64(tbase + TM_AGG, smem_u32(t1), true, smem_u32(base1 + TILE), true, true);
+        umma_commit(&bar_k[pi & 1]);
       }
       __syncwarp();
     }
     {
-      uint32_t ph = ((n1 - 1) >> 1) & 1;
-      if (!mbar_wait(&bar_k[(n1 - 1) & 1], ph)) ok = false;
+      const uint32_t ph = ((np - 1) >> 1) & 1;
+      if (!mbar_wait(&bar_k[(np - 1) & 1], ph)) ok = false;
     }
     tc_fence_after();
     tmem_ld_16x32(agg, tw + TM_AGG);
