@@ -432,9 +432,10 @@ def extra_affine(dev):
 def extra_backward(dev, B, H, T):
     """BASELINE config 2, backward: the reverse-time chunked tensor-core
     kernel on the forward's bf16 chunk states (two input sets alternated,
-    each > L2).  Algorithmic bytes per (token, head): q, k, v, do read
-    (4 x 128) + f (4) + chunk state (8192 / 64 = 128) + dq, dk, dv written
-    (3 x 128) + df (4) = 1032."""
+    each > L2).  Algorithmic bytes per (token, head): q, k, v, f, do read
+    (516) + dq, dk, dv, df written (388) = 904; the saved chunk states the
+    kernel also reads (8192 / 64 = 128 B per token and head) are reported
+    separately."""
     import torch
     from mogt_b200 import ops
     sets = []
@@ -455,9 +456,10 @@ def extra_backward(dev, B, H, T):
     e1.record()
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / n
-    alg = 1032 * B * H * T
+    alg = 904 * B * H * T
     return {"ms": ms, "tokens_per_s": B * T / (ms / 1e3), "GBps": alg / (ms / 1e3) / 1e9,
-            "algorithmic_bytes": alg, "dtype": "bf16 inputs, fp32 state/accumulate",
+            "algorithmic_bytes": alg, "chunk_state_bytes": 128 * B * H * T,
+            "dtype": "bf16 inputs, fp32 state/accumulate",
             "note": "includes the Python-side output allocation; forward with saved chunk states not timed"}
 
 
@@ -502,7 +504,7 @@ def extra_matrix(dev):
     M = torch.randn(B, H, T, d, d, generator=g, device=dev)
     W = 0.05 * (M - M.transpose(-1, -2))
     I = torch.eye(d, device=dev)
-    A = torch.linalg.solve(I - W, I + W)
+    A = torch.linalg.solve(I - W, I + W).contiguous()  # solve returns column-major batches
     del M, W
     q, k, v = (torch.randn(B, H, T, d, generator=g, device=dev).bfloat16() for _ in range(3))
     f = torch.sigmoid(torch.randn(B, H, T, generator=g, device=dev) + 2.0)
@@ -522,7 +524,7 @@ def extra_matrix(dev):
     torch.cuda.empty_cache()
     return {"ms": ms, "TFLOPs": units * 540672 / (ms / 1e3) / 1e12,
             "GBps": units * 16900 / (ms / 1e3) / 1e9,
-            "note": "fp32 SIMT (CUDA cores); A is 2.2 GB > L2"}
+            "note": "chunked: per-chunk [P | S_loc] fp32 SIMT (2x the minimal FMAs), carries per head, outputs per chunk; A is 2.2 GB > L2"}
 
 
 def extra_backbone(dev, world, rank):

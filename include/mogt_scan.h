@@ -144,6 +144,25 @@ int mogt_matrix_scan_fwd(const float* A, const void* q, const void* k, const voi
                          const float* f, void* o, const float* S0, float* S_final, int64_t BH,
                          int64_t T, int64_t d, int in_dtype, int out_dtype, void* stream);
 
+/* Chunked form of mogt_matrix_scan_fwd for long sequences (d = 64 only),
+ * with the same arguments, results and fp32 arithmetic plus:
+ *   status  : a zero-initialised 256-byte workspace header (the one the
+ *             gated-scan workspaces start with); a device-side wait that
+ *             gives up records MOGT_ERR_TIMEOUT there
+ *             (mogt_workspace_status reads it);
+ *   scratch : >= mogt_matrix_scan_chunked_scratch_bytes(BH, T, d) bytes,
+ *             16-byte aligned, any contents.
+ * T is split into 64-step chunks; every chunk's transition prefix products
+ * and local state run in parallel, the chunk carries are composed per head,
+ * and o = o_local + (P_t^T q_t)^T S_in is formed per chunk.  Any T >= 1.
+ * No counterpart in the reference beyond affine_scan.py:14-62, which this
+ * computes in another order. */
+size_t mogt_matrix_scan_chunked_scratch_bytes(int64_t BH, int64_t T, int64_t d);
+int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const void* k, const void* v,
+                                 const float* f, void* o, const float* S0, float* S_final,
+                                 int64_t BH, int64_t T, int64_t d, int in_dtype, int out_dtype,
+                                 void* status, void* scratch, size_t scratch_bytes, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).
  * Replaces triton_scan.py:232-311 (_triton_affine_scan_hybrid_forward: local

@@ -1,0 +1,419 @@
+// Chunked dense-transition headed scan (long sequences):
+//     S_t = A_t S_{t-1} + (1 - f_t) k_t v_t^T,      o_t = S_t^T q_t,
+// A_t: [BH, T, 64, 64] fp32, q, k, v: [BH, T, 64].  Same semantics as the
+// sequential kernel in matrix_scan.cu (affine_scan.py:14-62 with U_t = A_t,
+// V_t = (1-f_t) k_t v_t^T, then the readout einsum), reorganised so that the
+// whole sequence is not one dependency chain per head.
+//
+// Split T into chunks of 64 steps.  Inside chunk c (steps t0..t0+L-1), with
+// S_in the state entering it,
+//     S_t = P_t S_in + S^loc_t,   P_t = A_t ... A_{t0},
+//     S^loc_t = A_t S^loc_{t-1} + w_t k_t v_t^T  (S^loc_{t0-1} = 0),
+// so  o_t = S^loc_t^T q_t + S_in^T (P_t^T q_t).
+//
+// Kernel 1 (one CTA per head and chunk, all chunks in parallel) evolves the
+// 64 x 128 matrix X = [P | S^loc] through the chunk (X <- A_t X, plus the
+// rank-1 write in the S^loc half) and emits, per step, both readouts
+// u_t = P_t^T q_t and o^loc_t = S^loc_t^T q_t, and at the end P and S^loc.
+// This is 2x the multiply-adds of the plain recurrence, all of it in
+// independent CTAs.  fp32 FMAs: with norm-preserving A_t nothing is forgotten,
+// so round-off accumulates over the whole sequence and TF32 products drift.
+// Register tile: thread (warp w, half h, lane group g) owns rows
+// 4(2w+h)..+3 and columns 4g..+3 of both halves: per 4 contraction indices
+// it reads 4 float4 of A_t (two distinct rows per warp) and 8 float4 of X
+// (256 contiguous bytes per half-warp) for 128 FMAs.
+// Kernel 2 (one CTA per head and 8 state columns) composes the chunk carries
+// sequentially, S_in[c+1] = P_c S_in[c] + S^loc_c: 64^2 x 8 FMAs per chunk.
+// Kernel 3 (one CTA per head and chunk) forms o = o^loc + U S_in, U the
+// chunk's 64 x 64 matrix of u_t rows, and writes o in the output dtype.
+#include "common.cuh"
+
+namespace mogt {
+namespace mchunk {
+
+constexpr int D = 64;       // state rows (k index) and columns (v index)
+constexpr int C = 64;       // steps per chunk
+constexpr int NT = 256;     // threads of kernels 1 and 3
+constexpr int XP = 2 * D;   // row pitch of X = [P | S^loc] in floats
+constexpr int CC = 8;       // state columns per carry CTA
+
+template <typename TI>
+struct Slot {  // one step's inputs in shared memory: A_t, k_t, q_t, v_t
+  static constexpr int kBytesA = D * D * 4;
+  static constexpr int kRow = D * (int)sizeof(TI);
+  static constexpr int kBytes = kBytesA + 3 * kRow;
+  static_assert(kRow % 16 == 0 && kBytes % 16 == 0, "bulk copies need 16-byte sizes");
+};
+
+template <typename TI>
+constexpr size_t local_smem_bytes() {
+  return 2 * (size_t)Slot<TI>::kBytes + 2 * (size_t)D * XP * 4 + 2 * 8 * (size_t)XP * 4 + C * 4 + 16;
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ float4 ld4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+__device__ __forceinline__ float4 ld4(const __nv_bfloat16* p) {
+  const uint2 r = *reinterpret_cast<const uint2*>(p);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&r.y));
+  return make_float4(a.x, a.y, b.x, b.y);
+}
+__device__ __forceinline__ void st4(float* p, float a, float b, float c, float d) {
+  *reinterpret_cast<float4*>(p) = make_float4(a, b, c, d);
+}
+__device__ __forceinline__ float comp(const float4& v, int j) {
+  return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 1: per-chunk prefix products and local states with both readouts.
+// o_loc, u: [NB, C, D]; P_out, S_loc: [NB, D, D]; NB = BH * nch.
+// ---------------------------------------------------------------------------
+template <typename TI>
+__global__ void __launch_bounds__(NT, 2)
+    chunk_local_kernel(const float* __restrict__ A, const TI* __restrict__ q, const TI* __restrict__ k,
+                       const TI* __restrict__ v, const float* __restrict__ f, float* __restrict__ o_loc,
+                       float* __restrict__ u, float* __restrict__ P_out, float* __restrict__ S_loc, int T,
+                       int nch, WsHeader* hdr) {
+  using SL = Slot<TI>;
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* slots = smem_raw;                                             // [2][SL::kBytes]
+  float* X = reinterpret_cast<float*>(smem_raw + 2 * SL::kBytes);       // [2][D][XP]
+  float* red = X + 2 * D * XP;                                           // [2][8][XP]
+  float* fs = red + 2 * 8 * XP;                                          // [C]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(fs + C);                  // [2]
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int h = lane >> 4, g = lane & 15;
+  const int r0 = (2 * warp + h) * 4;  // this thread's rows r0..r0+3
+  const int c0 = g * 4;               // its columns c0..c0+3 of P and of S^loc
+  const int item = blockIdx.x;
+  const int bh = item / nch, c = item % nch;
+  const int t0 = c * C, L = min(C, T - t0);
+  const size_t row0 = (size_t)bh * T + t0;  // global step index of the chunk's first step
+
+  if (tid == 0) {
+    mbar_init(&bars[0], 1);
+    mbar_init(&bars[1], 1);
+    fence_barrier_init();
+  }
+  for (int e = tid; e < D * XP; e += NT) X[e] = (e % XP == e / XP) ? 1.f : 0.f;  // P = I, S^loc = 0
+  if (tid < C) fs[tid] = tid < L ? f[row0 + tid] : 1.f;
+  __syncthreads();
+
+  auto issue = [&](int s) {
+    if (s < L) {
+      uint8_t* sl = slots + (s & 1) * SL::kBytes;
+      const size_t r = row0 + s;
+      mbar_arrive_expect_tx(&bars[s & 1], SL::kBytes);
+      bulk_g2s(sl, A + r * D * D, SL::kBytesA, &bars[s & 1]);
+      bulk_g2s(sl + SL::kBytesA, k + r * D, SL::kRow, &bars[s & 1]);
+      bulk_g2s(sl + SL::kBytesA + SL::kRow, q + r * D, SL::kRow, &bars[s & 1]);
+      bulk_g2s(sl + SL::kBytesA + 2 * SL::kRow, v + r * D, SL::kRow, &bars[s & 1]);
+    }
+  };
+  if (tid == 0) issue(0);
+
+  float acc[4][8];
+  int cur = 0, s = 0;
+  bool ok = true;
+  for (; s < L; ++s) {
+    if (tid == 0) issue(s + 1);  // slot (s+1)&1 was last read before the previous step's barrier
+    if (!mbar_wait(&bars[s & 1], (s >> 1) & 1)) ok = false;
+    const uint8_t* sl = slots + (s & 1) * SL::kBytes;
+    const float* At = reinterpret_cast<const float*>(sl);
+    const TI* kt = reinterpret_cast<const TI*>(sl + SL::kBytesA);
+    const TI* qt = kt + D;
+    const TI* vt = qt + D;
+    const float* Xc = X + cur * D * XP;
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) acc[i][jj] = 0.f;
+#pragma unroll 2
+    for (int kk = 0; kk < D; kk += 4) {
+      float4 a[4], xp[4], xs[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = ld4(At + (r0 + i) * D + kk);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        xp[j] = ld4(Xc + (kk + j) * XP + c0);
+        xs[j] = ld4(Xc + (kk + j) * XP + D + c0);
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float aij = comp(a[i], j);
+          acc[i][0] = fmaf(aij, xp[j].x, acc[i][0]);
+          acc[i][1] = fmaf(aij, xp[j].y, acc[i][1]);
+          acc[i][2] = fmaf(aij, xp[j].z, acc[i][2]);
+          acc[i][3] = fmaf(aij, xp[j].w, acc[i][3]);
+          acc[i][4] = fmaf(aij, xs[j].x, acc[i][4]);
+          acc[i][5] = fmaf(aij, xs[j].y, acc[i][5]);
+          acc[i][6] = fmaf(aij, xs[j].z, acc[i][6]);
+          acc[i][7] = fmaf(aij, xs[j].w, acc[i][7]);
+        }
+    }
+    // rank-1 write into the S^loc half, formed as the reference forms V_t
+    const float w = 1.f - fs[s];
+    const float4 kr = ld4(kt + r0), vc = ld4(vt + c0), qr = ld4(qt + r0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][4 + j] += w * (comp(kr, i) * comp(vc, j));
+    float* Xn = X + (cur ^ 1) * D * XP;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      st4(Xn + (r0 + i) * XP + c0, acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      st4(Xn + (r0 + i) * XP + D + c0, acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+    }
+    // readouts: partial sums over this thread's 4 rows, then the warp's 8 rows
+    float part[8];
+#pragma unroll
+    for (int jj = 0; jj < 8; ++jj) {
+      float p = acc[0][jj] * qr.x;
+      p = fmaf(acc[1][jj], qr.y, p);
+      p = fmaf(acc[2][jj], qr.z, p);
+      p = fmaf(acc[3][jj], qr.w, p);
+      part[jj] = p + __shfl_xor_sync(0xffffffffu, p, 16);
+    }
+    float* rd = red + (s & 1) * 8 * XP + warp * XP;
+    if (h == 0) {
+      st4(rd + c0, part[0], part[1], part[2], part[3]);
+      st4(rd + D + c0, part[4], part[5], part[6], part[7]);
+    }
+    ok = __syncthreads_and(ok);
+    if (tid < XP) {
+      const float* rs = red + (s & 1) * 8 * XP + tid;
+      float sum = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < 8; ++ww) sum += rs[ww * XP];
+      float* dst = tid < D ? u : o_loc;
+      dst[((size_t)item * C + s) * D + (tid & (D - 1))] = sum;
+    }
+    cur ^= 1;
+    if (!ok) break;
+  }
+  if (ok) {
+    float* Pd = P_out + (size_t)item * D * D;
+    float* Sd = S_loc + (size_t)item * D * D;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      st4(Pd + (r0 + i) * D + c0, acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
+      st4(Sd + (r0 + i) * D + c0, acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+    }
+  } else if (tid == 0) {
+    record_error(hdr, MOGT_ERR_TIMEOUT, (uint32_t)item);
+    // the copy for step s+1 may still be in flight: let it land (bounded) before exit
+    if (s + 1 < L) mbar_wait(&bars[(s + 1) & 1], ((s + 1) >> 1) & 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 2: chunk carries S_in[c+1] = P_c S_in[c] + S^loc_c, per head and
+// CC-column group.  S_in: [NB, D, D] (S_in[0] = S0 or 0); S_final: [BH, D, D]
+// or NULL.  Thread layout: row tid/4, columns 2*(tid%4)..+1.
+// ---------------------------------------------------------------------------
+constexpr int CR = 3;  // ring slots for P_c
+__global__ void __launch_bounds__(256)
+    chunk_carry_kernel(const float* __restrict__ P, const float* __restrict__ S_loc,
+                       const float* __restrict__ S0, float* __restrict__ S_in, float* __restrict__ S_final,
+                       int nch, WsHeader* hdr) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  float* ring = reinterpret_cast<float*>(smem_raw);   // [CR][D][D]
+  float* St = ring + CR * D * D;                       // [2][D][CC]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(St + 2 * D * CC);
+  const int tid = threadIdx.x;
+  const int groups = D / CC;
+  const int bh = blockIdx.x / groups, cgp = blockIdx.x % groups;
+  const int r = tid >> 2, cl = (tid & 3) * 2, col = cgp * CC + cl;
+  const size_t item0 = (size_t)bh * nch;
+
+  if (tid == 0) {
+    for (int i = 0; i < CR; ++i) mbar_init(&bars[i], 1);
+    fence_barrier_init();
+  }
+  float2 s;
+  s.x = S0 ? S0[((size_t)bh * D + r) * D + col] : 0.f;
+  s.y = S0 ? S0[((size_t)bh * D + r) * D + col + 1] : 0.f;
+  *reinterpret_cast<float2*>(St + r * CC + cl) = s;
+  *reinterpret_cast<float2*>(S_in + (item0 * D + r) * D + col) = s;
+  __syncthreads();
+  auto issue = [&](int cc) {
+    if (cc < nch) {
+      mbar_arrive_expect_tx(&bars[cc % CR], D * D * 4);
+      bulk_g2s(ring + (cc % CR) * D * D, P + (item0 + cc) * D * D, D * D * 4, &bars[cc % CR]);
+    }
+  };
+  if (tid == 0)
+    for (int cc = 0; cc < CR - 1; ++cc) issue(cc);
+  float2 sl_next = *reinterpret_cast<const float2*>(S_loc + (item0 * D + r) * D + col);
+  bool ok = true;
+  int cur = 0, cc = 0;
+  for (; cc < nch; ++cc) {
+    if (tid == 0) issue(cc + CR - 1);
+    const float2 sl = sl_next;
+    if (cc + 1 < nch) sl_next = *reinterpret_cast<const float2*>(S_loc + ((item0 + cc + 1) * D + r) * D + col);
+    if (!mbar_wait(&bars[cc % CR], (cc / CR) & 1)) ok = false;
+    const float* Pc = ring + (cc % CR) * D * D + r * D;
+    const float* Sc = St + cur * D * CC + cl;
+    float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;  // two partial sums per column
+#pragma unroll
+    for (int kk = 0; kk < D; kk += 4) {
+      const float4 p = ld4(Pc + kk);
+      const float2 x0 = *reinterpret_cast<const float2*>(Sc + (kk + 0) * CC);
+      const float2 x1 = *reinterpret_cast<const float2*>(Sc + (kk + 1) * CC);
+      const float2 x2 = *reinterpret_cast<const float2*>(Sc + (kk + 2) * CC);
+      const float2 x3 = *reinterpret_cast<const float2*>(Sc + (kk + 3) * CC);
+      a0 = fmaf(p.x, x0.x, a0); a1 = fmaf(p.x, x0.y, a1);
+      b0 = fmaf(p.y, x1.x, b0); b1 = fmaf(p.y, x1.y, b1);
+      a0 = fmaf(p.z, x2.x, a0); a1 = fmaf(p.z, x2.y, a1);
+      b0 = fmaf(p.w, x3.x, b0); b1 = fmaf(p.w, x3.y, b1);
+    }
+    const float2 ns = make_float2((a0 + b0) + sl.x, (a1 + b1) + sl.y);
+    *reinterpret_cast<float2*>(St + (cur ^ 1) * D * CC + r * CC + cl) = ns;
+    if (cc + 1 < nch)
+      *reinterpret_cast<float2*>(S_in + ((item0 + cc + 1) * D + r) * D + col) = ns;
+    else if (S_final)
+      *reinterpret_cast<float2*>(S_final + ((size_t)bh * D + r) * D + col) = ns;
+    cur ^= 1;
+    ok = __syncthreads_and(ok);
+    if (!ok) break;
+  }
+  if (!ok && tid == 0) {
+    record_error(hdr, MOGT_ERR_TIMEOUT, (uint32_t)blockIdx.x);
+    for (int c2 = cc + 1; c2 < min(nch, cc + CR); ++c2) mbar_wait(&bars[c2 % CR], (c2 / CR) & 1);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel 3: o = o^loc + U S_in per chunk (U rows u_t), rows t < L written.
+// Thread layout: rows 4*(tid/16)..+3, columns 4*(tid%16)..+3.
+// ---------------------------------------------------------------------------
+template <typename TO>
+__global__ void __launch_bounds__(NT)
+    chunk_out_kernel(const float* __restrict__ o_loc, const float* __restrict__ u,
+                     const float* __restrict__ S_in, TO* __restrict__ o, int T, int nch) {
+  __shared__ __align__(16) float Us[C * D];
+  __shared__ __align__(16) float Ss[D * D];
+  const int tid = threadIdx.x;
+  const int item = blockIdx.x;
+  const int bh = item / nch, c = item % nch;
+  const int t0 = c * C, L = min(C, T - t0);
+  const float4* ug = reinterpret_cast<const float4*>(u + (size_t)item * C * D);
+  const float4* sg = reinterpret_cast<const float4*>(S_in + (size_t)item * D * D);
+  for (int e = tid; e < C * D / 4; e += NT) {
+    reinterpret_cast<float4*>(Us)[e] = ug[e];
+    reinterpret_cast<float4*>(Ss)[e] = sg[e];
+  }
+  const int rr = (tid >> 4) * 4, c0 = (tid & 15) * 4;
+  float acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float4 z = ld4(o_loc + ((size_t)item * C + rr + i) * D + c0);
+    acc[i][0] = z.x; acc[i][1] = z.y; acc[i][2] = z.z; acc[i][3] = z.w;
+  }
+  __syncthreads();
+#pragma unroll 4
+  for (int kk = 0; kk < D; kk += 4) {
+    float4 a[4], y[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) a[i] = ld4(Us + (rr + i) * D + kk);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) y[j] = ld4(Ss + (kk + j) * D + c0);
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float aij = comp(a[i], j);
+        acc[i][0] = fmaf(aij, y[j].x, acc[i][0]);
+        acc[i][1] = fmaf(aij, y[j].y, acc[i][1]);
+        acc[i][2] = fmaf(aij, y[j].z, acc[i][2]);
+        acc[i][3] = fmaf(aij, y[j].w, acc[i][3]);
+      }
+  }
+  TO* ob = o + ((size_t)bh * T + t0) * D;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    if (rr + i >= L) break;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) ob[(size_t)(rr + i) * D + c0 + j] = from_f32<TO>(acc[i][j]);
+  }
+}
+
+template <typename TI>
+int launch_local(const float* A, const void* q, const void* k, const void* v, const float* f, float* o_loc,
+                 float* u, float* P, float* S_loc, int NB, int T, int nch, WsHeader* hdr, cudaStream_t st) {
+  const size_t smem = local_smem_bytes<TI>();
+  auto kfn = chunk_local_kernel<TI>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+    return MOGT_ERR_LAUNCH;
+  kfn<<<NB, NT, smem, st>>>(A, static_cast<const TI*>(q), static_cast<const TI*>(k),
+                            static_cast<const TI*>(v), f, o_loc, u, P, S_loc, T, nch, hdr);
+  return mogt_host::launch_status();
+}
+
+}  // namespace mchunk
+}  // namespace mogt
+
+extern "C" size_t mogt_matrix_scan_chunked_scratch_bytes(int64_t BH, int64_t T, int64_t d) {
+  using namespace mogt::mchunk;
+  if (BH <= 0 || T <= 0 || d != D) return 0;
+  const int64_t nch = (T + C - 1) / C;
+  return (size_t)5 * BH * nch * D * D * 4;  // o_loc, u, P, S_loc, S_in
+}
+
+extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const void* k, const void* v,
+                                            const float* f, void* o, const float* S0, float* S_final,
+                                            int64_t BH, int64_t T, int64_t d, int in_dtype, int out_dtype,
+                                            void* status, void* scratch, size_t scratch_bytes,
+                                            void* stream) {
+  using namespace mogt::mchunk;
+  if (BH <= 0 || T < 0) return MOGT_ERR_SHAPE;
+  if (d != D) return MOGT_ERR_UNSUPPORTED;
+  if (T == 0) return MOGT_OK;
+  if (!A || !q || !k || !v || !f || !o || !status || !scratch) return MOGT_ERR_ARG;
+  const uintptr_t mis = reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(q) |
+                        reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+                        reinterpret_cast<uintptr_t>(scratch);
+  if (mis & 15u) return MOGT_ERR_ALIGN;
+  const int64_t nch = (T + C - 1) / C, NB = BH * nch;
+  if (NB >= ((int64_t)1 << 31) || BH * (D / CC) >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31))
+    return MOGT_ERR_UNSUPPORTED;
+  if (scratch_bytes < mogt_matrix_scan_chunked_scratch_bytes(BH, T, d)) return MOGT_ERR_WORKSPACE;
+  if (in_dtype != MOGT_DTYPE_BF16 && in_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+  if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+  if (in_dtype == MOGT_DTYPE_F32 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  auto* hdr = static_cast<mogt::WsHeader*>(status);
+  const size_t blk = (size_t)NB * D * D;
+  float* o_loc = static_cast<float*>(scratch);
+  float* u = o_loc + blk;
+  float* P = u + blk;
+  float* S_loc = P + blk;
+  float* S_in = S_loc + blk;
+  const int nb = (int)NB, Ti = (int)T, nc = (int)nch;
+  int rc = in_dtype == MOGT_DTYPE_BF16
+               ? launch_local<__nv_bfloat16>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st)
+               : launch_local<float>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st);
+  if (rc != MOGT_OK) return rc;
+  const size_t csmem = (size_t)CR * D * D * 4 + 2 * D * CC * 4 + 8 * CR;
+  if (cudaFuncSetAttribute(chunk_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem) !=
+      cudaSuccess)
+    return MOGT_ERR_LAUNCH;
+  chunk_carry_kernel<<<(unsigned)(BH * (D / CC)), 256, csmem, st>>>(P, S_loc, S0, S_in, S_final, nc, hdr);
+  if ((rc = mogt_host::launch_status()) != MOGT_OK) return rc;
+  if (out_dtype == MOGT_DTYPE_BF16)
+    chunk_out_kernel<__nv_bfloat16><<<nb, NT, 0, st>>>(o_loc, u, S_in, static_cast<__nv_bfloat16*>(o), Ti, nc);
+  else
+    chunk_out_kernel<float><<<nb, NT, 0, st>>>(o_loc, u, S_in, static_cast<float*>(o), Ti, nc);
+  return mogt_host::launch_status();
+}

@@ -129,10 +129,16 @@ def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False, chunk_
     return gq, gk, gv, gf, gS0
 
 
-def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False):
+def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False,
+                    chunked=None):
     """o_t = S_t^T q_t with S_t = A_t S_{t-1} + (1-f_t) k_t v_t^T (dense A_t).
     A: [B, H, T, d, d]; q, k, v: [B, H, T, d]; f: [B, H, T]; d in {16, 32, 64}.
-    Returns (o, S_final)."""
+    Returns (o, S_final).
+
+    d = 64 (the default for T > 64, `chunked=None`) runs the chunked kernels:
+    every 64-step chunk's transition prefix products and local state in
+    parallel, the chunk carries composed per head, then the outputs per chunk.
+    `chunked=False` forces the single sequential pass per head."""
     _require_cuda(A, q, k, v, f, initial_state, what="matrix_scan")
     if A.ndim != 5 or q.ndim != 4:
         raise ValueError("A must be [B, H, T, d, d] and q, k, v [B, H, T, d]")
@@ -144,16 +150,31 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
     out_dtype = output_dtype or q.dtype
     dev = q.device
     A = A.to(torch.float32).contiguous()
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    q, k, v = (t.contiguous() for t in (q, k, v))
     f = f.to(torch.float32).contiguous()
     S0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
     o = torch.empty(B, H, T, d, dtype=out_dtype, device=dev)
     S_fin = torch.empty(B, H, d, d, dtype=torch.float32, device=dev) if want_final else None
+    L = N.lib()
+    icode, ocode = N.dtype_code(q.dtype), N.dtype_code(out_dtype)
+    if chunked is None:
+        chunked = d == 64 and T > 64
+    if chunked and d != 64:
+        raise ValueError("the chunked matrix scan supports d = 64 only")
     with torch.cuda.device(dev):
-        st = N.lib().mogt_matrix_scan_fwd(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
-                                          N.ptr(S0), N.ptr(S_fin), B * H, T, d, N.dtype_code(q.dtype),
-                                          N.dtype_code(out_dtype), N.stream_ptr(dev))
-    N.check(st, "mogt_matrix_scan_fwd")
+        if not chunked:
+            st = L.mogt_matrix_scan_fwd(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
+                                        N.ptr(S0), N.ptr(S_fin), B * H, T, d, icode, ocode,
+                                        N.stream_ptr(dev))
+            N.check(st, "mogt_matrix_scan_fwd")
+            return o, S_fin
+        nbytes = L.mogt_matrix_scan_chunked_scratch_bytes(B * H, T, d)
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        status = N.workspaces.get(dev, 256)
+        st = L.mogt_matrix_scan_fwd_chunked(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
+                                            N.ptr(S0), N.ptr(S_fin), B * H, T, d, icode, ocode,
+                                            N.ptr(status), N.ptr(scratch), nbytes, N.stream_ptr(dev))
+        N.check(st, "mogt_matrix_scan_fwd_chunked")
     return o, S_fin
 
 

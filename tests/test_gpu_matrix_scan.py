@@ -64,7 +64,38 @@ def test_config3_full_length_split_consistency():
                                            output_dtype=torch.float32, want_final=True)
     o2, _ = mogt_b200.ops.matrix_scan_fwd(A[:, :, h:], q[:, :, h:], k[:, :, h:], v[:, :, h:], f[:, :, h:],
                                           initial_state=S1, output_dtype=torch.float32)
-    assert float((torch.cat([o1, o2], 2) - o).abs().max() / o.abs().max()) <= 1e-5
+    # the halves chunk at other boundaries (4000 is not a multiple of 64), so
+    # the sums are formed in another order: the fp32 bar, not bit equality
+    assert float((torch.cat([o1, o2], 2) - o).abs().max() / o.abs().max()) <= 1e-4
     oref = O.matrix_scan(*as64(A[:1, :2, :256], q[:1, :2, :256], k[:1, :2, :256], v[:1, :2, :256],
                                f[:1, :2, :256]))
     assert rel_max_err(o[:1, :2, :256].cpu().numpy(), oref) <= 1e-4
+
+
+@pytest.mark.parametrize("T", [1, 37, 64, 640, 1000])
+def test_chunked_vs_oracle_and_sequential(T):
+    """The chunked kernels (per-chunk prefix products and local states, chunk
+    carries, per-chunk outputs; ragged last chunk) against the oracle and the
+    single sequential pass."""
+    d = 64
+    import mogt_b200
+    g = torch.Generator().manual_seed(7 * d + T)
+    q, k, v = (torch.randn(1, 3, T, d, generator=g).bfloat16() for _ in range(3))
+    f = torch.sigmoid(torch.randn(1, 3, T, generator=g) + 2.0)
+    f[..., ::37] = 0.0
+    A = _cayley(1, 3, T, d, seed=T + 1)
+    S0 = torch.randn(1, 3, d, d, generator=g)
+    args = (A.cuda(), q.cuda(), k.cuda(), v.cuda(), f.cuda())
+    o, S = mogt_b200.ops.matrix_scan_fwd(*args, initial_state=S0.cuda(), output_dtype=torch.float32,
+                                         want_final=True, chunked=True)
+    o1, S1 = mogt_b200.ops.matrix_scan_fwd(*args, initial_state=S0.cuda(), output_dtype=torch.float32,
+                                           want_final=True, chunked=False)
+    assert rel_max_err(o.cpu().numpy(), o1.cpu().numpy()) <= 1e-4
+    assert rel_max_err(S.cpu().numpy(), S1.cpu().numpy()) <= 1e-4
+    Ad, qd, kd, vd, fd = as64(A, q, k, v, f)
+    U = np.concatenate([np.zeros((3, 1, d, d)), Ad.reshape(3, T, d, d)], 1)
+    Vin = (1 - fd.reshape(3, T))[..., None, None] * kd.reshape(3, T, d, 1) * vd.reshape(3, T, 1, d)
+    Vin = np.concatenate([S0.double().numpy().reshape(3, 1, d, d), Vin], 1)
+    Sref = O.affine_scan_sequential(U, Vin)[:, 1:]
+    oref = np.einsum("ntkv,ntk->ntv", Sref, qd.reshape(3, T, d)).reshape(1, 3, T, d)
+    assert rel_max_err(o.cpu().numpy(), oref) <= 1e-4
