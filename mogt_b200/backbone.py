@@ -26,7 +26,7 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
-from . import triton_scan
+from . import ops, triton_scan
 
 __all__ = ["RMSNorm", "SwiGLU", "MOGTBlock", "MOGTModel", "configure_identity_coupled"]
 
@@ -112,14 +112,47 @@ class MOGTBlock(nn.Module):
             parts.append(p.expand_as(x_norm))
         return parts[0] if len(parts) == 1 else torch.cat(parts, -1)
 
+    def _fused_identity_path(self, x, gate_lin):
+        """The identity connection with the forget gate coupled to the value
+        gate makes U_t diagonal: the scan and norm_out then run as one fused
+        kernel (mogt_diag_scan_norm_fwd) without materialising U or the fp32
+        states.  Forward-only: used when no gradient is recorded and the
+        default B200 scan is in use."""
+        return (getattr(self, "fused_identity_scan", True)
+                and getattr(self, "connection_impl", "matrix_exp") == "identity"
+                and gate_lin is not None
+                and getattr(self, "couple_forget_to_value_gate", False)
+                and self.scan_fn is _b200_scan
+                and x.is_cuda
+                and not torch.is_grad_enabled())
+
     def forward(self, x, prefix_condition=None):
         B, L, D = x.shape
         x_norm = self.norm_mogt(x)
+        gate_lin = getattr(self, "phi_value_gate", None)
+        if self._fused_identity_path(x, gate_lin):
+            with torch.autograd.profiler.record_function("mogt.value_projection"):
+                V = self.phi_val(x_norm).view(B, L, self.r, self.c)
+                z = gate_lin(self.value_gate_input(x_norm, prefix_condition)).float()
+                if z.size(-1) not in (1, self.r):
+                    raise ValueError("phi_value_gate must output 1 or r gates")
+                z = torch.sigmoid(z)
+            with torch.autograd.profiler.record_function("mogt.fused_scan_norm"):
+                # the readout GEMM consumes bf16 under bf16 autocast: write that directly
+                y_dtype = (torch.bfloat16 if torch.is_autocast_enabled("cuda")
+                           and torch.get_autocast_dtype("cuda") == torch.bfloat16 else torch.float32)
+                y, _ = ops.diag_scan_norm(V, z, self.norm_out.weight,
+                                          damping=float(getattr(self, "connection_damping", 0.999)),
+                                          eps=self.norm_out.eps, output_dtype=y_dtype)
+            with torch.autograd.profiler.record_function("mogt.readout"):
+                x = x + self.theta_read(y.view(B, L, D))
+            with torch.autograd.profiler.record_function("mogt.ffn"):
+                x = x + self.ffn(self.norm_ffn(x))
+            return x
         with torch.autograd.profiler.record_function("mogt.connection_map"):
             U = self.transport(x_norm)
         with torch.autograd.profiler.record_function("mogt.value_projection"):
             V = self.phi_val(x_norm).view(B, L, self.r, self.c)
-            gate_lin = getattr(self, "phi_value_gate", None)
             if gate_lin is not None:
                 z = gate_lin(self.value_gate_input(x_norm, prefix_condition)).float()
                 if z.size(-1) not in (1, self.r):

@@ -178,6 +178,46 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
     return o, S_fin
 
 
+def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=None,
+                   output_dtype=None, want_final=False):
+    """Fused identity-connection MOGT scan and RMSNorm readout:
+    h_t = damping (1 - z_t[row]) h_{t-1} + V_t z_t[row] per channel (V times z
+    rounded in V's dtype, as V * z.to(V.dtype) does), then per token
+    y_t = h_t * rsqrt(mean(h_t^2) + eps) * norm_weight.
+    V: [B, L, R, C] bf16/fp32; z: [B, L, R, 1] or [B, L, 1, 1] (or without
+    the last axis) fp32 gates; norm_weight: [R*C].  Returns (y [B, L, R*C],
+    H_final [B, R, C] fp32 or None)."""
+    _require_cuda(V, z, norm_weight, initial_state, what="diag_scan_norm")
+    if V.ndim != 4:
+        raise ValueError("V must be [B, L, R, C]")
+    B, L, R, C = V.shape
+    zz = z.reshape(B, L, -1) if z.numel() in (B * L, B * L * R) else None
+    if zz is None:
+        raise ValueError("z must hold one gate per token or one per row")
+    if V.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError("V must be bfloat16 or float32")
+    out_dtype = output_dtype or V.dtype
+    dev = V.device
+    V = V.contiguous()
+    zz = zz.to(torch.float32).contiguous()
+    w = norm_weight.to(torch.float32).contiguous()
+    if w.numel() != R * C:
+        raise ValueError("norm_weight must have R*C entries")
+    H0 = None if initial_state is None else initial_state.to(torch.float32).contiguous()
+    y = torch.empty(B, L, R * C, dtype=out_dtype, device=dev)
+    Hf = torch.empty(B, R, C, dtype=torch.float32, device=dev) if want_final else None
+    L_ = N.lib()
+    nbytes = L_.mogt_diag_scan_norm_scratch_bytes(B, L, R, C)
+    scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        st = L_.mogt_diag_scan_norm_fwd(N.ptr(V), N.ptr(zz), zz.shape[-1], float(damping), N.ptr(H0),
+                                        N.ptr(w), float(eps), N.ptr(y), N.ptr(Hf), B, L, R, C,
+                                        N.dtype_code(V.dtype), N.dtype_code(out_dtype), N.ptr(scratch),
+                                        scratch.numel(), N.stream_ptr(dev))
+    N.check(st, "mogt_diag_scan_norm_fwd")
+    return y, Hf
+
+
 def _check_uv(U, V):
     if U.ndim != 4 or V.ndim != 4:
         raise ValueError("U and V must be rank-4 tensors")
