@@ -126,6 +126,42 @@ class MOGTBlock(nn.Module):
                 and x.is_cuda
                 and not torch.is_grad_enabled())
 
+    def _gate_logits(self, x_norm, prefix, gate_lin):
+        """phi_value_gate(value_gate_input(x_norm, prefix)) without building
+        the concatenated [x_t, x_{t-1}, x_prefix] input: one GEMM of x_norm
+        against the current and previous-token weight blocks (fp32
+        accumulation), the previous-token part shifted by one step, the prefix
+        part once per sequence, the bias, then one rounding to the dtype the
+        concatenated linear would output (bf16 under bf16 autocast).  Equal to
+        the concatenated form up to fp32 summation order."""
+        mode = getattr(self, "value_gate_input_mode", "current")
+        B, L, D = x_norm.shape
+        prev, pre = "prev" in mode, "prefix" in mode
+        W = gate_lin.weight
+        if W.size(1) != (1 + prev + pre) * D:
+            return gate_lin(self.value_gate_input(x_norm, prefix)).float()
+        bf = torch.is_autocast_enabled("cuda") and torch.get_autocast_dtype("cuda") == torch.bfloat16
+        dt = torch.bfloat16 if bf else x_norm.dtype
+
+        def mm(a, w):
+            a, w = a.to(dt), w.to(dt)
+            with torch.autocast("cuda", enabled=False):
+                return torch.mm(a, w.t(), out_dtype=torch.float32) if bf else torch.mm(a, w.t()).float()
+
+        n = W.size(0)
+        wx = torch.cat([W[:, :D], W[:, D:2 * D]], 0) if prev else W[:, :D]
+        y = mm(x_norm.reshape(B * L, D), wx).view(B, L, -1)
+        logit = y[..., :n].clone()
+        if prev and L > 1:
+            logit[:, 1:] += y[:, :-1, n:]
+        if pre:
+            p = (torch.zeros(B, D, device=x_norm.device, dtype=x_norm.dtype) if prefix is None
+                 else prefix.to(x_norm.dtype).reshape(B, D))
+            logit += mm(p, W[:, (1 + prev) * D:])[:, None]
+        if gate_lin.bias is not None:
+            logit += gate_lin.bias.float()
+        return logit.to(dt).float() if bf else logit
+
     def forward(self, x, prefix_condition=None):
         B, L, D = x.shape
         x_norm = self.norm_mogt(x)
@@ -133,7 +169,7 @@ class MOGTBlock(nn.Module):
         if self._fused_identity_path(x, gate_lin):
             with torch.autograd.profiler.record_function("mogt.value_projection"):
                 V = self.phi_val(x_norm).view(B, L, self.r, self.c)
-                z = gate_lin(self.value_gate_input(x_norm, prefix_condition)).float()
+                z = self._gate_logits(x_norm, prefix_condition, gate_lin)
                 if z.size(-1) not in (1, self.r):
                     raise ValueError("phi_value_gate must output 1 or r gates")
                 z = torch.sigmoid(z)

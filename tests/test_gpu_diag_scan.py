@@ -103,3 +103,25 @@ def test_block_fused_path_matches_unfused():
         y_dense = m(ids).float()
     err = float((y_fused - y_dense).abs().max() / y_dense.abs().max())
     assert err <= 2e-2, err
+
+
+@pytest.mark.parametrize("mode", ["current", "current_prev", "current_prev_prefix"])
+def test_gate_logits_match_concatenated_linear(mode):
+    """The block's gate logits without the [x_t, x_{t-1}, x_prefix]
+    concatenation equal phi_value_gate on the concatenation, under bf16
+    autocast (one bf16 rounding apart at most) and in fp32."""
+    from mogt_b200.backbone import MOGTBlock
+    torch.manual_seed(3)
+    blk = MOGTBlock(256, 16).cuda()
+    mult = {"current": 1, "current_prev": 2, "current_prev_prefix": 3}[mode]
+    blk.phi_value_gate = torch.nn.Linear(mult * 256, 16).cuda()
+    blk.value_gate_input_mode = mode
+    x = torch.randn(2, 500, 256, device="cuda")
+    prefix = torch.randn(2, 256, device="cuda")
+    with torch.inference_mode():
+        for ac in (True, False):
+            with torch.autocast("cuda", dtype=torch.bfloat16, enabled=ac):
+                ref = blk.phi_value_gate(blk.value_gate_input(x, prefix)).float()
+                got = blk._gate_logits(x, prefix, blk.phi_value_gate)
+            tol = 1e-2 if ac else 1e-5
+            assert float((got - ref).abs().max()) <= tol * float(ref.abs().max()), (mode, ac)
