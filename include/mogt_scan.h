@@ -172,19 +172,23 @@ int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const void* k, c
  * norm_out(H):
  *   h_t = damping (1 - z_t[row]) h_{t-1} + v_t z_t[row]  per channel,
  *   y_t = h_t * rsqrt(mean(h_t^2) + eps) * norm_weight   per token.
- *   V : [B, L, R, C] bf16 or f32 (8-byte aligned); z : [B, L, z_per_token]
+ *   V : [B, L, R, C] bf16 or f32 (16-byte aligned); z : [B, L, z_per_token]
  *   f32 with z_per_token = R (row-wise gate) or 1 (one gate);
  *   H0 : [B, R, C] f32 initial state or NULL; norm_weight : [R*C] f32;
  *   y : [B, L, R*C] in out_dtype (bf16 or f32); H_final : [B, R, C] f32 or
- *   NULL.  C even, R*C a multiple of 64 and <= 2048.
- *   scratch : >= mogt_diag_scan_norm_scratch_bytes(B, L, R, C) bytes.
+ *   NULL.  C even, R*C a multiple of 64 and <= 2048, R <= 64.
+ *   status  : a zero-initialised 256-byte workspace header; a device-side
+ *             wait that gives up records MOGT_ERR_TIMEOUT there;
+ *   scratch : >= mogt_diag_scan_norm_scratch_bytes(B, L, R, C, in_dtype)
+ *             bytes, 16-byte aligned.
  * ------------------------------------------------------------------------- */
-size_t mogt_diag_scan_norm_scratch_bytes(int64_t B, int64_t L, int64_t R, int64_t C);
+size_t mogt_diag_scan_norm_scratch_bytes(int64_t B, int64_t L, int64_t R, int64_t C,
+                                         int in_dtype);
 int mogt_diag_scan_norm_fwd(const void* V, const float* z, int64_t z_per_token, float damping,
                             const float* H0, const float* norm_weight, float eps, void* y,
                             float* H_final, int64_t B, int64_t L, int64_t R, int64_t C,
-                            int in_dtype, int out_dtype, void* scratch, size_t scratch_bytes,
-                            void* stream);
+                            int in_dtype, int out_dtype, void* status, void* scratch,
+                            size_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).

@@ -207,13 +207,14 @@ def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=No
     y = torch.empty(B, L, R * C, dtype=out_dtype, device=dev)
     Hf = torch.empty(B, R, C, dtype=torch.float32, device=dev) if want_final else None
     L_ = N.lib()
-    nbytes = L_.mogt_diag_scan_norm_scratch_bytes(B, L, R, C)
+    nbytes = L_.mogt_diag_scan_norm_scratch_bytes(B, L, R, C, N.dtype_code(V.dtype))
     scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+    status = N.workspaces.get(dev, 256)
     with torch.cuda.device(dev):
         st = L_.mogt_diag_scan_norm_fwd(N.ptr(V), N.ptr(zz), zz.shape[-1], float(damping), N.ptr(H0),
                                         N.ptr(w), float(eps), N.ptr(y), N.ptr(Hf), B, L, R, C,
-                                        N.dtype_code(V.dtype), N.dtype_code(out_dtype), N.ptr(scratch),
-                                        scratch.numel(), N.stream_ptr(dev))
+                                        N.dtype_code(V.dtype), N.dtype_code(out_dtype), N.ptr(status),
+                                        N.ptr(scratch), scratch.numel(), N.stream_ptr(dev))
     N.check(st, "mogt_diag_scan_norm_fwd")
     return y, Hf
 

@@ -125,3 +125,15 @@ def test_gate_logits_match_concatenated_linear(mode):
                 got = blk._gate_logits(x, prefix, blk.phi_value_gate)
             tol = 1e-2 if ac else 1e-5
             assert float((got - ref).abs().max()) <= tol * float(ref.abs().max()), (mode, ac)
+
+
+def test_wide_fp32_short_chunks():
+    """D = 2048 fp32: the V tile budget cuts chunks to 8 tokens (pieces of 2
+    tokens, shorter than a normalisation group); ragged L."""
+    from mogt_b200 import ops
+    B, L, R, C = 2, 101, 32, 64
+    V, z, w = _inputs(B, L, R, C, torch.float32, True, seed=12)
+    y, Hf = ops.diag_scan_norm(V.cuda(), z.cuda(), w.cuda(), damping=0.99, want_final=True)
+    yr, Hr = _reference(V, z, w, 0.99, 1e-6)
+    assert rel_max_err(y.cpu().numpy(), yr) <= 1e-4
+    assert rel_max_err(Hf.cpu().numpy(), Hr) <= 1e-4
