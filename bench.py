@@ -42,6 +42,8 @@ def parse():
     p.add_argument("--batch", type=int, default=1)
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--no-extra", action="store_true")
+    p.add_argument("--profile-case", choices=sorted(PROFILE_CASES),
+                   help="run one named workload three times on cuda:0 and exit (for ncu captures)")
     return p.parse_args()
 
 
@@ -276,12 +278,12 @@ def run_b200(args):
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     t_wall0 = time.perf_counter()
     e0.record(stream)
+    # clocks are sampled by the sampler's own thread only: a synchronous NVML
+    # query here would stall the launches and leave the GPU idle inside the
+    # timed region when few steps are queued
     for i in range(args.steps):
         step(i)
-        if i == args.steps // 2:
-            clocks.sample("mid")
     e1.record(stream)
-    clocks.sample("enqueued")
     torch.cuda.synchronize()
     t_wall1 = time.perf_counter()
     if world > 1:
@@ -571,8 +573,81 @@ def extra_backbone(dev, world, rank):
             "reference_L4_2layer_B1_tokens_per_s": 422000}
 
 
+def _cayley_transitions(B, H, T, d, dev, seed):
+    """Config-3 transitions A_t = solve(I - W_t, I + W_t), W_t = 0.05 (M - M^T)."""
+    import torch
+    g = torch.Generator(device=dev).manual_seed(seed)
+    M = torch.randn(B, H, T, d, d, generator=g, device=dev)
+    W = 0.05 * (M - M.transpose(-1, -2))
+    I = torch.eye(d, device=dev)
+    return torch.linalg.solve(I - W, I + W).contiguous()
+
+
+def _case_fwd_config2(dev):
+    from mogt_b200 import ops
+    q, k, v, f = (t.to(dev) for t in make_inputs(1, 12, 32768, 0))
+    return lambda: ops.gated_scan_fwd(q, k, v, f)
+
+
+def _case_bwd_config2(dev):
+    import torch
+    from mogt_b200 import ops
+    q, k, v, f = (t.to(dev) for t in make_inputs(1, 12, 32768, 0))
+    g = torch.randn(1, 12, 32768, 64, device=dev).bfloat16()
+    _, _, _, cs = ops.gated_scan_fwd(q, k, v, f, save_states=True)
+    return lambda: ops.gated_scan_bwd(q, k, v, f, g, chunk_states=cs)
+
+
+def _case_matrix(B, H, T):
+    def make(dev):
+        import torch
+        from mogt_b200 import ops
+        A = _cayley_transitions(B, H, T, 64, dev, 11)
+        g = torch.Generator(device=dev).manual_seed(12)
+        q, k, v = (torch.randn(B, H, T, 64, generator=g, device=dev).bfloat16() for _ in range(3))
+        f = torch.sigmoid(torch.randn(B, H, T, generator=g, device=dev) + 2.0)
+        return lambda: ops.matrix_scan_fwd(A, q, k, v, f)
+    return make
+
+
+def _case_diag(B, L):
+    def make(dev):
+        import torch
+        from mogt_b200 import ops
+        g = torch.Generator(device=dev).manual_seed(0)
+        V = torch.randn(B, L, 16, 48, generator=g, device=dev).bfloat16()
+        z = torch.sigmoid(torch.randn(B, L, 16, 1, generator=g, device=dev) - 2.0)
+        w = torch.ones(768, device=dev)
+        return lambda: ops.diag_scan_norm(V, z, w, output_dtype=torch.bfloat16)
+    return make
+
+
+# name -> builder of a zero-argument call; each case runs the call three times
+PROFILE_CASES = {
+    "fwd_config2": _case_fwd_config2,                 # gated forward, B=1 H=12 T=32768
+    "bwd_config2": _case_bwd_config2,                 # gated backward on saved chunk states
+    "matrix_config3": _case_matrix(2, 8, 8192),       # dense transitions, A = 2.2 GB
+    "matrix_small": _case_matrix(1, 16, 2048),        # 512 chunk CTAs, A = 537 MB
+    "diag_backbone": _case_diag(8, 32768),            # fused diagonal scan + norm, backbone shape
+    "diag_small": _case_diag(8, 16384),
+}
+
+
+def run_profile_case(name):
+    import torch
+    dev = torch.device("cuda", 0)
+    call = PROFILE_CASES[name](dev)
+    for _ in range(3):
+        call()
+    torch.cuda.synchronize()
+    print(f"profile case {name}: 3 calls done")
+    return 0
+
+
 def main():
     args = parse()
+    if args.profile_case:
+        return run_profile_case(args.profile_case)
     if args.impl == "reference":
         return run_reference(args)
     return run_b200(args)
