@@ -21,7 +21,9 @@
 // Register tile: thread (warp w, half h, lane group g) owns rows
 // 4(2w+h)..+3 and columns 4g..+3 of both halves: per 4 contraction indices
 // it reads 4 float4 of A_t (two distinct rows per warp) and 8 float4 of X
-// (256 contiguous bytes per half-warp) for 128 FMAs.
+// (256 contiguous bytes per half-warp) for 128 FMAs, issued as 64 packed
+// fma.rn.f32x2 on (even k, odd k) pairs -- the kernel is issue bound, and the
+// packed form does the same FMA work in half the instructions.
 // Kernel 2 (one CTA per head and 8 state columns) composes the chunk carries
 // sequentially, S_in[c+1] = P_c S_in[c] + S^loc_c: 64^2 x 8 FMAs per chunk.
 // Kernel 3 (one CTA per head and chunk) forms o = o^loc + U S_in, U the
@@ -71,6 +73,30 @@ __device__ __forceinline__ void st4(float* p, float a, float b, float c, float d
 __device__ __forceinline__ float comp(const float4& v, int j) {
   return j == 0 ? v.x : j == 1 ? v.y : j == 2 ? v.z : v.w;
 }
+// d = a * b + c on fp32 pairs (one packed FMA instruction for two lanes of work)
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;"
+      : "=l"(d)
+      : "l"(*reinterpret_cast<const uint64_t*>(&a)), "l"(*reinterpret_cast<const uint64_t*>(&b)),
+        "l"(*reinterpret_cast<const uint64_t*>(&c)));
+  return *reinterpret_cast<const float2*>(&d);
+}
+__device__ __forceinline__ float2 lo2(const float4& v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(const float4& v) { return make_float2(v.z, v.w); }
+
+// Shared-memory layout of X = [P | S^loc] (64 x 128), interleaved by pairs of
+// rows (the contraction index k) so that one float4 holds
+// (X[2kp][c], X[2kp+1][c], X[2kp][c+1], X[2kp+1][c+1]): the operand pair of
+// two packed FMAs that accumulate even and odd k separately.  Row pair kp
+// holds 256 floats in four 64-float blocks (P columns 4g, 4g+1 | P 4g+2, 4g+3
+// | the same two for S^loc), lane group g's float4 at 4g inside each block,
+// so a half-warp's loads of one block are 256 contiguous bytes.
+__device__ __forceinline__ int xidx(int k, int c) {
+  const int cc = c & 63, g = cc >> 2, w = cc & 3;
+  const int blk = (c >> 6) * 2 + (w >> 1);
+  return (k >> 1) * 256 + blk * 64 + g * 4 + (w & 1) * 2 + (k & 1);
+}
 
 // ---------------------------------------------------------------------------
 // Kernel 1: per-chunk prefix products and local states with both readouts.
@@ -104,7 +130,10 @@ __global__ void __launch_bounds__(NT, 2)
     mbar_init(&bars[1], 1);
     fence_barrier_init();
   }
-  for (int e = tid; e < D * XP; e += NT) X[e] = (e % XP == e / XP) ? 1.f : 0.f;  // P = I, S^loc = 0
+  for (int e = tid; e < D * XP; e += NT) {  // P = I, S^loc = 0
+    const int kr = e / XP, c = e % XP;
+    X[xidx(kr, c)] = (c == kr) ? 1.f : 0.f;
+  }
   if (tid < C) fs[tid] = tid < L ? f[row0 + tid] : 1.f;
   __syncthreads();
 
@@ -132,36 +161,39 @@ __global__ void __launch_bounds__(NT, 2)
     const TI* kt = reinterpret_cast<const TI*>(sl + SL::kBytesA);
     const TI* qt = kt + D;
     const TI* vt = qt + D;
-    const float* Xc = X + cur * D * XP;
+    const float* Xc = X + cur * D * XP + g * 4;
+    float2 acc2[4][8];  // (even-k, odd-k) partial sums
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int jj = 0; jj < 8; ++jj) acc[i][jj] = 0.f;
+      for (int jj = 0; jj < 8; ++jj) acc2[i][jj] = make_float2(0.f, 0.f);
 #pragma unroll 2
     for (int kk = 0; kk < D; kk += 4) {
-      float4 a[4], xp[4], xs[4];
+      float4 a[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) a[i] = ld4(At + (r0 + i) * D + kk);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        xp[j] = ld4(Xc + (kk + j) * XP + c0);
-        xs[j] = ld4(Xc + (kk + j) * XP + D + c0);
-      }
+      for (int m = 0; m < 2; ++m) {
+        const float* xr = Xc + (kk / 2 + m) * 256;
+        const float4 x0 = ld4(xr), x1 = ld4(xr + 64), x2 = ld4(xr + 128), x3 = ld4(xr + 192);
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float aij = comp(a[i], j);
-          acc[i][0] = fmaf(aij, xp[j].x, acc[i][0]);
-          acc[i][1] = fmaf(aij, xp[j].y, acc[i][1]);
-          acc[i][2] = fmaf(aij, xp[j].z, acc[i][2]);
-          acc[i][3] = fmaf(aij, xp[j].w, acc[i][3]);
-          acc[i][4] = fmaf(aij, xs[j].x, acc[i][4]);
-          acc[i][5] = fmaf(aij, xs[j].y, acc[i][5]);
-          acc[i][6] = fmaf(aij, xs[j].z, acc[i][6]);
-          acc[i][7] = fmaf(aij, xs[j].w, acc[i][7]);
+        for (int i = 0; i < 4; ++i) {
+          const float2 ap = m == 0 ? lo2(a[i]) : hi2(a[i]);  // (A[r][k], A[r][k+1])
+          acc2[i][0] = ffma2(ap, lo2(x0), acc2[i][0]);
+          acc2[i][1] = ffma2(ap, hi2(x0), acc2[i][1]);
+          acc2[i][2] = ffma2(ap, lo2(x1), acc2[i][2]);
+          acc2[i][3] = ffma2(ap, hi2(x1), acc2[i][3]);
+          acc2[i][4] = ffma2(ap, lo2(x2), acc2[i][4]);
+          acc2[i][5] = ffma2(ap, hi2(x2), acc2[i][5]);
+          acc2[i][6] = ffma2(ap, lo2(x3), acc2[i][6]);
+          acc2[i][7] = ffma2(ap, hi2(x3), acc2[i][7]);
         }
+      }
     }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int jj = 0; jj < 8; ++jj) acc[i][jj] = acc2[i][jj].x + acc2[i][jj].y;
     // rank-1 write into the S^loc half, formed as the reference forms V_t
     const float w = 1.f - fs[s];
     const float4 kr = ld4(kt + r0), vc = ld4(vt + c0), qr = ld4(qt + r0);
@@ -169,11 +201,16 @@ __global__ void __launch_bounds__(NT, 2)
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][4 + j] += w * (comp(kr, i) * comp(vc, j));
-    float* Xn = X + (cur ^ 1) * D * XP;
+    float* Xn = X + (cur ^ 1) * D * XP + g * 4;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      st4(Xn + (r0 + i) * XP + c0, acc[i][0], acc[i][1], acc[i][2], acc[i][3]);
-      st4(Xn + (r0 + i) * XP + D + c0, acc[i][4], acc[i][5], acc[i][6], acc[i][7]);
+    for (int m = 0; m < 2; ++m) {  // rows r0 + 2m, r0 + 2m + 1 form row pair r0/2 + m
+      float* xw = Xn + (r0 / 2 + m) * 256;
+      const float* e0 = acc[2 * m];
+      const float* e1 = acc[2 * m + 1];
+      st4(xw, e0[0], e1[0], e0[1], e1[1]);
+      st4(xw + 64, e0[2], e1[2], e0[3], e1[3]);
+      st4(xw + 128, e0[4], e1[4], e0[5], e1[5]);
+      st4(xw + 192, e0[6], e1[6], e0[7], e1[7]);
     }
     // readouts: partial sums over this thread's 4 rows, then the warp's 8 rows
     float part[8];
