@@ -257,21 +257,28 @@ __global__ void __launch_bounds__(NT, 2)
 // ---------------------------------------------------------------------------
 // Kernel 2: chunk carries S_in[c+1] = P_c S_in[c] + S^loc_c, per head and
 // CC-column group.  S_in: [NB, D, D] (S_in[0] = S0 or 0); S_final: [BH, D, D]
-// or NULL.  Thread layout: row tid/4, columns 2*(tid%4)..+1.
+// or NULL.  Thread layout: row r = tid/4 (j = r % 8 inside the warp), columns
+// 2*(tid%4)..+1.  The state lives column-major in shared memory (pitch SP) so
+// that a thread reads four k values of a column with one float4, and each
+// lane group starts its k loop 4j further on: the 8 rows of P_c a warp reads
+// at once then fall in 8 different bank groups.  P_c arrives through a CR-slot
+// bulk-copy ring, S^loc_c through registers four chunks ahead.
 // ---------------------------------------------------------------------------
-constexpr int CR = 3;  // ring slots for P_c
+constexpr int CR = 6;        // ring slots for P_c
+constexpr int SP = D + 4;    // column pitch of the state in shared memory
+constexpr int SLA = 4;       // S^loc chunks loaded ahead
 __global__ void __launch_bounds__(256)
     chunk_carry_kernel(const float* __restrict__ P, const float* __restrict__ S_loc,
                        const float* __restrict__ S0, float* __restrict__ S_in, float* __restrict__ S_final,
                        int nch, WsHeader* hdr) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   float* ring = reinterpret_cast<float*>(smem_raw);   // [CR][D][D]
-  float* St = ring + CR * D * D;                       // [2][D][CC]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(St + 2 * D * CC);
+  float* St = ring + CR * D * D;                       // [2][CC][SP]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(St + 2 * CC * SP);
   const int tid = threadIdx.x;
   const int groups = D / CC;
   const int bh = blockIdx.x / groups, cgp = blockIdx.x % groups;
-  const int r = tid >> 2, cl = (tid & 3) * 2, col = cgp * CC + cl;
+  const int r = tid >> 2, jr = r & 7, cl = (tid & 3) * 2, col = cgp * CC + cl;
   const size_t item0 = (size_t)bh * nch;
 
   if (tid == 0) {
@@ -281,7 +288,8 @@ __global__ void __launch_bounds__(256)
   float2 s;
   s.x = S0 ? S0[((size_t)bh * D + r) * D + col] : 0.f;
   s.y = S0 ? S0[((size_t)bh * D + r) * D + col + 1] : 0.f;
-  *reinterpret_cast<float2*>(St + r * CC + cl) = s;
+  St[cl * SP + r] = s.x;
+  St[(cl + 1) * SP + r] = s.y;
   *reinterpret_cast<float2*>(S_in + (item0 * D + r) * D + col) = s;
   __syncthreads();
   auto issue = [&](int cc) {
@@ -292,31 +300,41 @@ __global__ void __launch_bounds__(256)
   };
   if (tid == 0)
     for (int cc = 0; cc < CR - 1; ++cc) issue(cc);
-  float2 sl_next = *reinterpret_cast<const float2*>(S_loc + (item0 * D + r) * D + col);
+  auto load_sl = [&](int cc) {
+    return cc < nch ? *reinterpret_cast<const float2*>(S_loc + ((item0 + cc) * D + r) * D + col)
+                    : make_float2(0.f, 0.f);
+  };
+  float2 slq[SLA];
+#pragma unroll
+  for (int u = 0; u < SLA; ++u) slq[u] = load_sl(u);
   bool ok = true;
   int cur = 0, cc = 0;
   for (; cc < nch; ++cc) {
     if (tid == 0) issue(cc + CR - 1);
-    const float2 sl = sl_next;
-    if (cc + 1 < nch) sl_next = *reinterpret_cast<const float2*>(S_loc + ((item0 + cc + 1) * D + r) * D + col);
+    const float2 sl = slq[0];
+#pragma unroll
+    for (int u = 0; u + 1 < SLA; ++u) slq[u] = slq[u + 1];
+    slq[SLA - 1] = load_sl(cc + SLA);
     if (!mbar_wait(&bars[cc % CR], (cc / CR) & 1)) ok = false;
     const float* Pc = ring + (cc % CR) * D * D + r * D;
-    const float* Sc = St + cur * D * CC + cl;
+    const float* S0c = St + cur * CC * SP + cl * SP;
+    const float* S1c = S0c + SP;
     float a0 = 0.f, a1 = 0.f, b0 = 0.f, b1 = 0.f;  // two partial sums per column
 #pragma unroll
     for (int kk = 0; kk < D; kk += 4) {
-      const float4 p = ld4(Pc + kk);
-      const float2 x0 = *reinterpret_cast<const float2*>(Sc + (kk + 0) * CC);
-      const float2 x1 = *reinterpret_cast<const float2*>(Sc + (kk + 1) * CC);
-      const float2 x2 = *reinterpret_cast<const float2*>(Sc + (kk + 2) * CC);
-      const float2 x3 = *reinterpret_cast<const float2*>(Sc + (kk + 3) * CC);
-      a0 = fmaf(p.x, x0.x, a0); a1 = fmaf(p.x, x0.y, a1);
-      b0 = fmaf(p.y, x1.x, b0); b1 = fmaf(p.y, x1.y, b1);
-      a0 = fmaf(p.z, x2.x, a0); a1 = fmaf(p.z, x2.y, a1);
-      b0 = fmaf(p.w, x3.x, b0); b1 = fmaf(p.w, x3.y, b1);
+      const int kq = (kk + 4 * jr) & (D - 1);
+      const float4 p = ld4(Pc + kq);
+      const float4 x = ld4(S0c + kq);
+      const float4 y = ld4(S1c + kq);
+      a0 = fmaf(p.x, x.x, a0); a1 = fmaf(p.x, y.x, a1);
+      b0 = fmaf(p.y, x.y, b0); b1 = fmaf(p.y, y.y, b1);
+      a0 = fmaf(p.z, x.z, a0); a1 = fmaf(p.z, y.z, a1);
+      b0 = fmaf(p.w, x.w, b0); b1 = fmaf(p.w, y.w, b1);
     }
     const float2 ns = make_float2((a0 + b0) + sl.x, (a1 + b1) + sl.y);
-    *reinterpret_cast<float2*>(St + (cur ^ 1) * D * CC + r * CC + cl) = ns;
+    float* Sn = St + (cur ^ 1) * CC * SP;
+    Sn[cl * SP + r] = ns.x;
+    Sn[(cl + 1) * SP + r] = ns.y;
     if (cc + 1 < nch)
       *reinterpret_cast<float2*>(S_in + ((item0 + cc + 1) * D + r) * D + col) = ns;
     else if (S_final)
@@ -442,7 +460,7 @@ extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const
                ? launch_local<__nv_bfloat16>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st)
                : launch_local<float>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st);
   if (rc != MOGT_OK) return rc;
-  const size_t csmem = (size_t)CR * D * D * 4 + 2 * D * CC * 4 + 8 * CR;
+  const size_t csmem = (size_t)CR * D * D * 4 + 2 * CC * SP * 4 + 8 * CR;
   if (cudaFuncSetAttribute(chunk_carry_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)csmem) !=
       cudaSuccess)
     return MOGT_ERR_LAUNCH;
