@@ -526,7 +526,7 @@ def extra_matrix(dev):
     torch.cuda.empty_cache()
     return {"ms": ms, "TFLOPs": units * 540672 / (ms / 1e3) / 1e12,
             "GBps": units * 16900 / (ms / 1e3) / 1e9,
-            "note": "chunked: per-chunk [P | S_loc] fp32 SIMT (2x the minimal FMAs), carries per head, outputs per chunk; A is 2.2 GB > L2"}
+            "note": "chunked: per-chunk [P | S_loc] evolved on tcgen05 tensor cores (3xTF32, fp32-level accuracy; 2x the minimal FLOP), carries per head, outputs per chunk; A is 2.2 GB > L2"}
 
 
 def extra_backbone(dev, world, rank):

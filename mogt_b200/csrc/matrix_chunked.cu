@@ -404,6 +404,275 @@ __global__ void __launch_bounds__(NT)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Kernel 1, tensor-core form (bf16 q/k/v): the same per-chunk recurrence and
+// outputs as chunk_local_kernel, with X <- A_t X computed on the tensor cores
+// as Y <- Y A_t^T for Y = X^T (M = 128 columns of X, N = 64, K = 64).  fp32
+// accuracy from three tf32 products (3xTF32): A ~ Ah + Al and Y ~ Yh + Yl
+// with Ah = rna_tf32(A), Al = rna_tf32(A - Ah) (A - Ah is exact in fp32),
+// likewise for Y; Y A^T ~ Yh Ah^T + Yh Al^T + Yl Ah^T.  The remainders'
+// rounding and the dropped Yl Al^T are ~2^-22 relative and unbiased (the
+// tensor core would truncate a non-tf32 remainder, and that bias accumulates
+// linearly over a norm-preserving sequence).  The products accumulate in three
+// tensor-memory accumulators -- Yh Ah^T over k < 32, over k >= 32, and the two
+// cross terms -- added in fp32 in the epilogue: the large terms then see 4
+// accumulation steps per step instead of 24, which keeps the accumulator's
+// rounding from building up over the sequence.  Per step: TMA brings A_t (two 32-column halves, 128B swizzle,
+// K-major: A's row-major rows are the B operand's N rows) and bulk copies
+// k_t, q_t, v_t; all threads split A_t in place into Ah and an Al tile; one
+// thread issues 24 kind::tf32 MMAs into a 128 x 64 fp32 accumulator in
+// tensor memory; then warp w reads lanes 32 (w % 4) + l (column c of X) and
+// accumulator columns 32 (w / 4) .. +31 (rows r of X), adds the rank-1 write
+// on the S^loc half, forms the readout partial sums, and writes Y's new
+// hi / lo rows (128-byte swizzled, the next step's A operand).
+// ---------------------------------------------------------------------------
+namespace tc {
+constexpr int OFF_A = 0;                   // A_t (Ah after the split): [2 halves][64 rows][128 B]
+constexpr int OFF_AL = OFF_A + 16384;      // Al: [2 halves][64][128 B]
+constexpr int OFF_YH = OFF_AL + 16384;     // Yh: [2 halves][128 rows][128 B]
+constexpr int OFF_YL = OFF_YH + 32768;     // Yl
+constexpr int OFF_KQV = OFF_YL + 32768;    // [2 slots][k, q, v rows] (<= 3 x 256 B each)
+constexpr int OFF_RED = OFF_KQV + 2 * 768; // [2 halves][128] readout partial sums
+constexpr int OFF_FS = OFF_RED + 1024;     // gates of the chunk [64]
+constexpr int OFF_BAR = OFF_FS + 256;      // A slots [2], MMA [1], TMEM address slot
+constexpr int SMEM = OFF_BAR + 64;
+constexpr int SMEM_ALLOC = SMEM + 1024;    // 1024-byte alignment of the swizzled tiles
+constexpr uint32_t IDESC = (1u << 4) | (2u << 7) | (2u << 10) | ((64u >> 3) << 17) | ((128u >> 4) << 24);
+
+__device__ __forceinline__ void umma_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, bool accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"((uint32_t)accumulate));
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int32_t c0,
+                                            int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+// x rounded to the nearest tf32 value (an fp32 bit pattern with a zero low
+// 13-bit field, which the tensor core takes as is)
+__device__ __forceinline__ float tf32_rna(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return __uint_as_float(r);
+}
+}  // namespace tc
+
+template <typename TI>
+__global__ void __launch_bounds__(NT, 2)
+    chunk_local_tc(const __grid_constant__ CUtensorMap tA, const TI* __restrict__ q, const TI* __restrict__ k,
+                   const TI* __restrict__ v, const float* __restrict__ f, float* __restrict__ o_loc,
+                   float* __restrict__ u, float* __restrict__ P_out, float* __restrict__ S_loc, int T, int nch,
+                   WsHeader* hdr) {
+  using namespace tc;
+  constexpr int KROW = D * (int)sizeof(TI);
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* sm = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* red = reinterpret_cast<float*>(sm + OFF_RED);
+  float* fs = reinterpret_cast<float*>(sm + OFF_FS);
+  uint64_t* bar_a = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
+  uint64_t* bar_m = bar_a + 2;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_a + 3);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int lq = warp & 3, hh = warp >> 2;
+  const int cx = 32 * lq + lane;  // column of X (row of Y) this thread reads back
+  const int item = blockIdx.x;
+  const int bh = item / nch, c = item % nch;
+  const int t0 = c * C, L = min(C, T - t0);
+  const size_t row0 = (size_t)bh * T + t0;
+
+  if (warp == 0) tmem_alloc(tslot, 256);  // three 64-column accumulators
+  if (tid == 0) {
+    mbar_init(&bar_a[0], 1);
+    mbar_init(&bar_a[1], 1);
+    mbar_init(bar_m, 1);
+    fence_barrier_init();
+  }
+  // Y = X^T at the chunk start: P = I (rows c < 64 of Y), S^loc = 0; Yl = 0
+  for (int e = tid; e < 2 * 128 * 8; e += NT) {
+    const int half = e >> 10, row = (e >> 3) & 127, ch = e & 7;
+    float4 hv = make_float4(0.f, 0.f, 0.f, 0.f);
+    const int kb = 32 * half + 4 * ch;  // first k of the 16-byte chunk
+    if (row < 64 && row >= kb && row < kb + 4) reinterpret_cast<float*>(&hv)[row - kb] = 1.f;
+    const uint32_t off = half * 16384 + sw128(row, ch);
+    *reinterpret_cast<float4*>(sm + OFF_YH + off) = hv;
+    *reinterpret_cast<float4*>(sm + OFF_YL + off) = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  if (tid < C) fs[tid] = tid < L ? f[row0 + tid] : 1.f;
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+
+  // A_t into the single A tile (free once step st-1's MMAs are complete),
+  // k_t, q_t, v_t into row slot st & 1 (the epilogue of step st-1 still
+  // reads the other one)
+  auto issue = [&](int st) {
+    if (st < L) {
+      const int sl = st & 1;
+      uint8_t* a = sm + OFF_A;
+      uint8_t* kq = sm + OFF_KQV + sl * 768;
+      const size_t r = row0 + st;
+      mbar_arrive_expect_tx(&bar_a[sl], 16384 + 3 * KROW);
+      tma_load_2d(a, &tA, &bar_a[sl], 0, (int32_t)(r * D));
+      tma_load_2d(a + 8192, &tA, &bar_a[sl], 32, (int32_t)(r * D));
+      bulk_g2s(kq, k + r * D, KROW, &bar_a[sl]);
+      bulk_g2s(kq + KROW, q + r * D, KROW, &bar_a[sl]);
+      bulk_g2s(kq + 2 * KROW, v + r * D, KROW, &bar_a[sl]);
+    }
+  };
+  if (tid == 0) issue(0);
+
+  float x[32];
+  bool ok = true;
+  int s = 0;
+  for (; s < L; ++s) {
+    const int sl = s & 1;
+    if (!mbar_wait(&bar_a[sl], (s >> 1) & 1)) ok = false;
+    // split A_t in place into Ah, and Al into its own tile (same layout)
+    {
+      float4* a4 = reinterpret_cast<float4*>(sm + OFF_A);
+      float4* l4 = reinterpret_cast<float4*>(sm + OFF_AL);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 a = a4[tid + NT * i];
+        const float4 h = make_float4(tf32_rna(a.x), tf32_rna(a.y), tf32_rna(a.z), tf32_rna(a.w));
+        a4[tid + NT * i] = h;
+        l4[tid + NT * i] = make_float4(tf32_rna(a.x - h.x), tf32_rna(a.y - h.y), tf32_rna(a.z - h.z),
+                                       tf32_rna(a.w - h.w));
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      const uint32_t ya = smem_u32(sm + OFF_YH), yl = smem_u32(sm + OFF_YL);
+      const uint32_t ah = smem_u32(sm + OFF_A), al = smem_u32(sm + OFF_AL);
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int half = kk >> 2;
+        const uint64_t sub = 2u * (kk & 3);  // 32 bytes per K=8 step, in 16-byte units
+        const uint64_t dyh = umma_desc_kmajor(ya + half * 16384) + sub;
+        const uint64_t dyl = umma_desc_kmajor(yl + half * 16384) + sub;
+        const uint64_t dah = umma_desc_kmajor(ah + half * 8192) + sub;
+        const uint64_t dal = umma_desc_kmajor(al + half * 8192) + sub;
+        umma_tf32(tbase + 64u * half, dyh, dah, (kk & 3) != 0);  // Yh Ah^T, per k-half
+        umma_tf32(tbase + 128u, dyh, dal, kk > 0);                // cross terms
+        umma_tf32(tbase + 128u, dyl, dah, true);
+      }
+      umma_commit(bar_m);
+    }
+    if (!mbar_wait(bar_m, s & 1)) ok = false;
+    tc_fence_after();
+    if (tid == 0) issue(s + 1);  // the A tile is free: its MMAs are complete; lands during the epilogue
+    {
+      const uint32_t ta = tbase + ((uint32_t)(32 * lq) << 16) + 32u * hh;
+      uint32_t r0[32];
+      tmem_ld_32x32b_x32_async(r0, ta);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] = __uint_as_float(r0[j]);
+      tmem_ld_32x32b_x32_async(r0, ta + 64u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] += __uint_as_float(r0[j]);
+      tmem_ld_32x32b_x32_async(r0, ta + 128u);
+      tmem_wait_ld();
+#pragma unroll
+      for (int j = 0; j < 32; ++j) x[j] += __uint_as_float(r0[j]);
+    }
+    const TI* kt = reinterpret_cast<const TI*>(sm + OFF_KQV + sl * 768);
+    const TI* qt = kt + D;
+    const TI* vt = qt + D;
+    if (cx >= D) {  // rank-1 write into the S^loc half, formed as the reference forms V_t
+      const float w = 1.f - fs[s];
+      const float vc = to_f32(vt[cx - D]);
+#pragma unroll
+      for (int j = 0; j < 32; j += 4) {
+        const float4 k4 = ld4(kt + 32 * hh + j);
+        x[j] += w * (k4.x * vc);
+        x[j + 1] += w * (k4.y * vc);
+        x[j + 2] += w * (k4.z * vc);
+        x[j + 3] += w * (k4.w * vc);
+      }
+    }
+    float part = 0.f;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      const float4 q4 = ld4(qt + 32 * hh + j);
+      part = fmaf(x[j], q4.x, part);
+      part = fmaf(x[j + 1], q4.y, part);
+      part = fmaf(x[j + 2], q4.z, part);
+      part = fmaf(x[j + 3], q4.w, part);
+    }
+    red[hh * 128 + cx] = part;
+    // the new Y row cx, k-half hh: hi and lo parts, 128-byte swizzled
+    {
+      uint8_t* yh = sm + OFF_YH + hh * 16384;
+      uint8_t* ylo = sm + OFF_YL + hh * 16384;
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {
+        const float4 hv = make_float4(tf32_rna(x[4 * ch]), tf32_rna(x[4 * ch + 1]), tf32_rna(x[4 * ch + 2]),
+                                      tf32_rna(x[4 * ch + 3]));
+        *reinterpret_cast<float4*>(yh + sw128(cx, ch)) = hv;
+        *reinterpret_cast<float4*>(ylo + sw128(cx, ch)) =
+            make_float4(tf32_rna(x[4 * ch] - hv.x), tf32_rna(x[4 * ch + 1] - hv.y),
+                        tf32_rna(x[4 * ch + 2] - hv.z), tf32_rna(x[4 * ch + 3] - hv.w));
+      }
+    }
+    fence_proxy_async();
+    tc_fence_before();
+    ok = __syncthreads_and(ok);
+    if (tid < 128) {
+      const float sum = red[tid] + red[128 + tid];
+      float* dst = tid < D ? u : o_loc;
+      dst[((size_t)item * C + s) * D + (tid & (D - 1))] = sum;
+    }
+    if (!ok) break;
+  }
+  if (ok) {  // the chunk's P and S^loc: column cx of X, rows 32 hh .. +31
+    float* dst = (cx < D ? P_out : S_loc) + (size_t)item * D * D + (cx & (D - 1));
+#pragma unroll
+    for (int j = 0; j < 32; ++j) dst[(size_t)(32 * hh + j) * D] = x[j];
+  } else if (tid == 0) {
+    record_error(hdr, MOGT_ERR_TIMEOUT, (uint32_t)item);
+    mbar_wait(bar_m, s & 1);  // let this step's MMAs and the next step's copies finish
+    if (s + 1 < L) mbar_wait(&bar_a[(s + 1) & 1], ((s + 1) >> 1) & 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 256);
+  }
+}
+
+int launch_local_tc(const float* A, const void* q, const void* k, const void* v, const float* f, float* o_loc,
+                    float* u, float* P, float* S_loc, int BH, int NB, int T, int nch, WsHeader* hdr,
+                    cudaStream_t st) {
+  CUtensorMap map;
+  cuuint64_t dims[2] = {(cuuint64_t)D, (cuuint64_t)BH * T * D};
+  cuuint64_t strides[1] = {(cuuint64_t)D * 4};
+  cuuint32_t box[2] = {32, (cuuint32_t)D};
+  if (mogt_host::encode_tiled(&map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(A), dims, strides,
+                              box, CU_TENSOR_MAP_SWIZZLE_128B) != CUDA_SUCCESS)
+    return MOGT_ERR_LAUNCH;
+  auto kfn = chunk_local_tc<__nv_bfloat16>;
+  if (cudaFuncSetAttribute(kfn, cudaFuncAttributeMaxDynamicSharedMemorySize, tc::SMEM_ALLOC) != cudaSuccess)
+    return MOGT_ERR_LAUNCH;
+  kfn<<<NB, NT, tc::SMEM_ALLOC, st>>>(map, static_cast<const __nv_bfloat16*>(q),
+                                      static_cast<const __nv_bfloat16*>(k), static_cast<const __nv_bfloat16*>(v),
+                                      f, o_loc, u, P, S_loc, T, nch, hdr);
+  return mogt_host::launch_status();
+}
+
 template <typename TI>
 int launch_local(const float* A, const void* q, const void* k, const void* v, const float* f, float* o_loc,
                  float* u, float* P, float* S_loc, int NB, int T, int nch, WsHeader* hdr, cudaStream_t st) {
@@ -456,8 +725,10 @@ extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const
   float* S_loc = P + blk;
   float* S_in = S_loc + blk;
   const int nb = (int)NB, Ti = (int)T, nc = (int)nch;
+  // bf16 inputs: the tensor-core (3xTF32) chunk kernel; fp32 inputs keep the
+  // fp32-FMA kernel
   int rc = in_dtype == MOGT_DTYPE_BF16
-               ? launch_local<__nv_bfloat16>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st)
+               ? launch_local_tc(A, q, k, v, f, o_loc, u, P, S_loc, (int)BH, nb, Ti, nc, hdr, st)
                : launch_local<float>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st);
   if (rc != MOGT_OK) return rc;
   const size_t csmem = (size_t)CR * D * D * 4 + 2 * CC * SP * 4 + 8 * CR;
