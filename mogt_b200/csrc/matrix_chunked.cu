@@ -29,6 +29,7 @@
 // Kernel 3 (one CTA per head and chunk) forms o = o^loc + U S_in, U the
 // chunk's 64 x 64 matrix of u_t rows, and writes o in the output dtype.
 #include "common.cuh"
+#include "trace.cuh"
 
 namespace mogt {
 namespace mchunk {
@@ -427,9 +428,12 @@ __global__ void __launch_bounds__(NT)
 // hi / lo rows (128-byte swizzled, the next step's A operand).
 // ---------------------------------------------------------------------------
 namespace tc {
-constexpr int OFF_A = 0;                   // A_t (Ah after the split): [2 halves][64 rows][128 B]
-constexpr int OFF_AL = OFF_A + 16384;      // Al: [2 halves][64][128 B]
-constexpr int OFF_YH = OFF_AL + 16384;     // Yh: [2 halves][128 rows][128 B]
+// Two A tiles ([2 halves][64 rows][128 B] each) swap roles every step: A_s
+// arrives in tile s & 1 and is split there into Ah, Al goes to the other
+// tile; once the Yh Al^T products of step s are complete that tile is free
+// and A_{s+1} is loaded into it while the rest of step s runs.
+constexpr int OFF_A = 0;
+constexpr int OFF_YH = OFF_A + 2 * 16384;  // Yh: [2 halves][128 rows][128 B]
 constexpr int OFF_YL = OFF_YH + 32768;     // Yl
 constexpr int OFF_KQV = OFF_YL + 32768;    // [2 slots][k, q, v rows] (<= 3 x 256 B each)
 constexpr int OFF_RED = OFF_KQV + 2 * 768; // [2 halves][128] readout partial sums
@@ -475,8 +479,9 @@ __global__ void __launch_bounds__(NT, 2)
   float* red = reinterpret_cast<float*>(sm + OFF_RED);
   float* fs = reinterpret_cast<float*>(sm + OFF_FS);
   uint64_t* bar_a = reinterpret_cast<uint64_t*>(sm + OFF_BAR);
-  uint64_t* bar_m = bar_a + 2;
-  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_a + 3);
+  uint64_t* bar_m = bar_a + 2;   // all products of a step
+  uint64_t* bar_lo = bar_a + 3;  // the Yh Al^T products of a step (the Al tile is free)
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(bar_a + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int lq = warp & 3, hh = warp >> 2;
@@ -491,6 +496,7 @@ __global__ void __launch_bounds__(NT, 2)
     mbar_init(&bar_a[0], 1);
     mbar_init(&bar_a[1], 1);
     mbar_init(bar_m, 1);
+    mbar_init(bar_lo, 1);
     fence_barrier_init();
   }
   // Y = X^T at the chunk start: P = I (rows c < 64 of Y), S^loc = 0; Yl = 0
@@ -510,13 +516,13 @@ __global__ void __launch_bounds__(NT, 2)
   tc_fence_after();
   const uint32_t tbase = *tslot;
 
-  // A_t into the single A tile (free once step st-1's MMAs are complete),
-  // k_t, q_t, v_t into row slot st & 1 (the epilogue of step st-1 still
-  // reads the other one)
+  // A_st into A tile st & 1 (step st-1's Al tile, free once its Yh Al^T
+  // products are complete), k_st, q_st, v_st into row slot st & 1 (the
+  // epilogue of step st-1 still reads the other one)
   auto issue = [&](int st) {
     if (st < L) {
       const int sl = st & 1;
-      uint8_t* a = sm + OFF_A;
+      uint8_t* a = sm + OFF_A + sl * 16384;
       uint8_t* kq = sm + OFF_KQV + sl * 768;
       const size_t r = row0 + st;
       mbar_arrive_expect_tx(&bar_a[sl], 16384 + 3 * KROW);
@@ -534,11 +540,13 @@ __global__ void __launch_bounds__(NT, 2)
   int s = 0;
   for (; s < L; ++s) {
     const int sl = s & 1;
+    MOGT_CLK(item, 0, s == 10);
     if (!mbar_wait(&bar_a[sl], (s >> 1) & 1)) ok = false;
+    MOGT_CLK(item, 1, s == 10);
     // split A_t in place into Ah, and Al into its own tile (same layout)
     {
-      float4* a4 = reinterpret_cast<float4*>(sm + OFF_A);
-      float4* l4 = reinterpret_cast<float4*>(sm + OFF_AL);
+      float4* a4 = reinterpret_cast<float4*>(sm + OFF_A + sl * 16384);
+      float4* l4 = reinterpret_cast<float4*>(sm + OFF_A + (sl ^ 1) * 16384);
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const float4 a = a4[tid + NT * i];
@@ -551,27 +559,39 @@ __global__ void __launch_bounds__(NT, 2)
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
+    MOGT_CLK(item, 2, s == 10);
     if (tid == 0) {
       tc_fence_after();
       const uint32_t ya = smem_u32(sm + OFF_YH), yl = smem_u32(sm + OFF_YL);
-      const uint32_t ah = smem_u32(sm + OFF_A), al = smem_u32(sm + OFF_AL);
+      const uint32_t ah = smem_u32(sm + OFF_A + sl * 16384), al = smem_u32(sm + OFF_A + (sl ^ 1) * 16384);
+      // 32 bytes per K=8 step, in 16-byte units of the descriptor's address field
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {  // cross term Yh Al^T first: it frees the Al tile
+        const int half = kk >> 2;
+        const uint64_t sub = 2u * (kk & 3);
+        umma_tf32(tbase + 128u, umma_desc_kmajor(ya + half * 16384) + sub,
+                  umma_desc_kmajor(al + half * 8192) + sub, kk > 0);
+      }
+      umma_commit(bar_lo);
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const int half = kk >> 2;
-        const uint64_t sub = 2u * (kk & 3);  // 32 bytes per K=8 step, in 16-byte units
-        const uint64_t dyh = umma_desc_kmajor(ya + half * 16384) + sub;
-        const uint64_t dyl = umma_desc_kmajor(yl + half * 16384) + sub;
+        const uint64_t sub = 2u * (kk & 3);
         const uint64_t dah = umma_desc_kmajor(ah + half * 8192) + sub;
-        const uint64_t dal = umma_desc_kmajor(al + half * 8192) + sub;
-        umma_tf32(tbase + 64u * half, dyh, dah, (kk & 3) != 0);  // Yh Ah^T, per k-half
-        umma_tf32(tbase + 128u, dyh, dal, kk > 0);                // cross terms
-        umma_tf32(tbase + 128u, dyl, dah, true);
+        umma_tf32(tbase + 64u * half, umma_desc_kmajor(ya + half * 16384) + sub, dah,
+                  (kk & 3) != 0);                                                         // Yh Ah^T per k-half
+        umma_tf32(tbase + 128u, umma_desc_kmajor(yl + half * 16384) + sub, dah, true);  // cross term Yl Ah^T
       }
       umma_commit(bar_m);
+      MOGT_CLK(item, 3, s == 10);
+      // A_{s+1} goes into the Al tile as soon as the products reading it are done
+      if (mbar_wait(bar_lo, s & 1)) issue(s + 1);
+      else ok = false;
+      MOGT_CLK(item, 4, s == 10);
     }
     if (!mbar_wait(bar_m, s & 1)) ok = false;
     tc_fence_after();
-    if (tid == 0) issue(s + 1);  // the A tile is free: its MMAs are complete; lands during the epilogue
+    MOGT_CLK(item, 5, s == 10);
     {
       const uint32_t ta = tbase + ((uint32_t)(32 * lq) << 16) + 32u * hh;
       uint32_t r0[32];
@@ -588,6 +608,7 @@ __global__ void __launch_bounds__(NT, 2)
 #pragma unroll
       for (int j = 0; j < 32; ++j) x[j] += __uint_as_float(r0[j]);
     }
+    MOGT_CLK(item, 6, s == 10);
     const TI* kt = reinterpret_cast<const TI*>(sm + OFF_KQV + sl * 768);
     const TI* qt = kt + D;
     const TI* vt = qt + D;
@@ -627,9 +648,11 @@ __global__ void __launch_bounds__(NT, 2)
                         tf32_rna(x[4 * ch + 2] - hv.z), tf32_rna(x[4 * ch + 3] - hv.w));
       }
     }
+    MOGT_CLK(item, 7, s == 10);
     fence_proxy_async();
     tc_fence_before();
     ok = __syncthreads_and(ok);
+    MOGT_CLK(item, 8, s == 10);
     if (tid < 128) {
       const float sum = red[tid] + red[128 + tid];
       float* dst = tid < D ? u : o_loc;
@@ -743,3 +766,7 @@ extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const
     chunk_out_kernel<float><<<nb, NT, 0, st>>>(o_loc, u, S_in, static_cast<float*>(o), Ti, nc);
   return mogt_host::launch_status();
 }
+
+#ifdef MOGT_TRACE
+extern "C" int mogt_debug_set_trace_matrix(void* buf) { return mogt::set_trace(buf); }
+#endif
