@@ -153,8 +153,10 @@ int mogt_matrix_scan_fwd(const float* A, const void* q, const void* k, const voi
  *   scratch : >= mogt_matrix_scan_chunked_scratch_bytes(BH, T, d) bytes,
  *             16-byte aligned, any contents.
  * T is split into 64-step chunks; every chunk's transition prefix products
- * and local state run in parallel, the chunk carries are composed per head,
- * and o = o_local + (P_t^T q_t)^T S_in is formed per chunk.  Any T >= 1.
+ * and local state run in parallel (bf16 q/k/v: on the tensor cores, three
+ * tf32 products per step for fp32-level accuracy; fp32 q/k/v: fp32 FMAs),
+ * the chunk carries are composed per head, and o = o_local +
+ * (P_t^T q_t)^T S_in is formed per chunk.  Any T >= 1.
  * No counterpart in the reference beyond affine_scan.py:14-62, which this
  * computes in another order. */
 size_t mogt_matrix_scan_chunked_scratch_bytes(int64_t BH, int64_t T, int64_t d);

@@ -137,7 +137,9 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
 
     d = 64 (the default for T > 64, `chunked=None`) runs the chunked kernels:
     every 64-step chunk's transition prefix products and local state in
-    parallel, the chunk carries composed per head, then the outputs per chunk.
+    parallel (bf16 q/k/v on the tensor cores with three tf32 products per
+    step, fp32 q/k/v with fp32 FMAs), the chunk carries composed per head,
+    then the outputs per chunk.
     `chunked=False` forces the single sequential pass per head."""
     _require_cuda(A, q, k, v, f, initial_state, what="matrix_scan")
     if A.ndim != 5 or q.ndim != 4:
