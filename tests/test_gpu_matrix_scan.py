@@ -72,15 +72,17 @@ def test_config3_full_length_split_consistency():
     assert rel_max_err(o[:1, :2, :256].cpu().numpy(), oref) <= 1e-4
 
 
-@pytest.mark.parametrize("T", [1, 37, 64, 640, 1000])
-def test_chunked_vs_oracle_and_sequential(T):
-    """The chunked kernels (per-chunk prefix products and local states, chunk
-    carries, per-chunk outputs; ragged last chunk) against the oracle and the
-    single sequential pass."""
+@pytest.mark.parametrize("T,dtype", [(1, torch.bfloat16), (37, torch.bfloat16), (64, torch.bfloat16),
+                                     (640, torch.bfloat16), (1000, torch.bfloat16), (640, torch.float32)])
+def test_chunked_vs_oracle_and_sequential(T, dtype):
+    """The chunked kernels (per-chunk prefix products and local states on the
+    tensor cores for bf16 q/k/v, fp32 FMAs for fp32; chunk carries, per-chunk
+    outputs; ragged last chunk) against the oracle and the single sequential
+    pass."""
     d = 64
     import mogt_b200
     g = torch.Generator().manual_seed(7 * d + T)
-    q, k, v = (torch.randn(1, 3, T, d, generator=g).bfloat16() for _ in range(3))
+    q, k, v = (torch.randn(1, 3, T, d, generator=g).to(dtype) for _ in range(3))
     f = torch.sigmoid(torch.randn(1, 3, T, generator=g) + 2.0)
     f[..., ::37] = 0.0
     A = _cayley(1, 3, T, d, seed=T + 1)
