@@ -414,12 +414,11 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       }
       tc_fence_after();
       MOGT_CLK(unit, 6, c == 5);
-      // all tensor-memory reads of this iteration in flight together
+      // the P and dS accumulators are read together
       const bool need_ds = c + 1 < nc || (final_here && p.S_final);
       uint32_t r_ds[16], r_p[16], r_o[16];
       if (need_ds) tmem_ld_16x32_async(r_ds, tw + TM_DS);
       if (want_out) tmem_ld_16x32_async(r_p, tw + TM_P);
-      if (want_out && c > 0) tmem_ld_16x32_async(r_o, tw + TM_O0 + 64u * ((c - 1) & 1));
       tmem_wait_ld();
       MOGT_CLK(unit, 14, c == 5);
       // state for chunk c+1 (or the final state)
@@ -446,8 +445,13 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         }
       }
       MOGT_CLK(unit, 15, c == 5);
-      // output of the previous chunk
-      if (want_out && c > 0) write_out_regs(c - 1, r_o);
+      // output of the previous chunk, read back only now: with all three
+      // accumulators in flight at once the kernel spills at its 128-register cap
+      if (want_out && c > 0) {
+        tmem_ld_16x32_async(r_o, tw + TM_O0 + 64u * ((c - 1) & 1));
+        tmem_wait_ld();
+        write_out_regs(c - 1, r_o);
+      }
       MOGT_CLK(unit, 7, c == 5);
       // P'_c: causal mask (and the exact decays when they do not factorise)
       if (want_out) {
