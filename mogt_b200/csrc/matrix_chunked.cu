@@ -16,9 +16,11 @@
 // rank-1 write in the S^loc half) and emits, per step, both readouts
 // u_t = P_t^T q_t and o^loc_t = S^loc_t^T q_t, and at the end P and S^loc.
 // This is 2x the multiply-adds of the plain recurrence, all of it in
-// independent CTAs.  fp32 FMAs: with norm-preserving A_t nothing is forgotten,
-// so round-off accumulates over the whole sequence and TF32 products drift.
-// Register tile: thread (warp w, half h, lane group g) owns rows
+// independent CTAs.  With norm-preserving A_t nothing is forgotten, so
+// round-off accumulates over the whole sequence and the state is kept at
+// fp32 accuracy: bf16 q/k/v use chunk_local_tc (tensor cores, three tf32
+// products per step, described at that kernel); fp32 q/k/v use
+// chunk_local_kernel (fp32 FMAs).  chunk_local_kernel's register tile: thread (warp w, half h, lane group g) owns rows
 // 4(2w+h)..+3 and columns 4g..+3 of both halves: per 4 contraction indices
 // it reads 4 float4 of A_t (two distinct rows per warp) and 8 float4 of X
 // (256 contiguous bytes per half-warp) for 128 FMAs, issued as 64 packed
