@@ -241,9 +241,9 @@ def run_b200(args):
     world, rank, local = dist_env()
     if world > 1:
         # NCCL's own messages (its version line, and whatever NCCL_DEBUG asks
-        # for) go to stderr unless the caller chose a file: stdout carries only
-        # the JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+        # for) go to a per-process file unless the caller chose one: stdout
+        # carries only the JSON line
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/mogt_bench_nccl.%h.%p.log")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     else:
