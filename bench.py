@@ -240,10 +240,14 @@ def run_b200(args):
 
     world, rank, local = dist_env()
     if world > 1:
-        # NCCL's own messages (its version line, and whatever NCCL_DEBUG asks
-        # for) go to a per-process file unless the caller chose one: stdout
-        # carries only the JSON line
-        os.environ.setdefault("NCCL_DEBUG_FILE", "/tmp/mogt_bench_nccl.%h.%p.log")
+        # what the C++ side prints (the communicator's NCCL version line among
+        # it) goes to stderr: file descriptor 1 is pointed at stderr and Python's
+        # stdout keeps a duplicate of the original, so stdout carries only the
+        # JSON line
+        sys.stdout.flush()
+        out_fd = os.dup(1)
+        os.dup2(2, 1)
+        sys.stdout = os.fdopen(out_fd, "w", buffering=1)
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", device_id=torch.device("cuda", local))
     else:
