@@ -206,19 +206,12 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside)}
 
 
-def profile_traffic():
-    """DRAM traffic per launch of the forward kernel from the committed ncu
-    summary (a line 'traffic_bytes_per_launch: N'), or None."""
-    p = ROOT / "profiles" / "gated_fwd_tc_config2_T32768.md"
-    if not p.exists():
-        return None
-    for line in p.read_text().splitlines():
-        if line.strip().startswith("traffic_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].strip())
-            except ValueError:
-                return None
-    return None
+# DRAM bytes (read + write) of one launch of the forward kernel at the bench
+# workload, from one ncu capture of that launch (dram__bytes_read.sum +
+# dram__bytes_write.sum; the command is in the forward kernel's profile
+# summary).  Updated by hand when the kernel changes; None when no capture
+# of the current kernel exists.
+FWD_TRAFFIC_BYTES_PER_LAUNCH = 258156800
 
 
 def measured_peak_hbm():
@@ -384,7 +377,7 @@ def run_b200(args):
     peak, peak_kind = measured_peak_hbm()
     alg_bytes = BYTES_PER_TOKEN_HEAD * B * H * T
     achieved = alg_bytes / (ms_per_step / 1e3) / 1e9
-    traffic = profile_traffic()
+    traffic = FWD_TRAFFIC_BYTES_PER_LAUNCH
     line = {
         "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,

@@ -97,15 +97,24 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
  * 16 MiB array built into the library, which every GPU that loads the library
  * keeps for the life of the process (enough for BASELINE-sized problems such
  * as 12 heads x 32768 steps; larger requests return MOGT_ERR_TOO_LARGE and
- * do nothing).  The first call on a device looks up that device's copy of
- * the array (make it before any stream capture); no call allocates.  All
- * calls share the one array and each call clears the part that must start
- * at zero, so calls whose GPU work overlaps (other streams, other host
- * threads) race and must be serialised by the caller. */
+ * do nothing; every argument is checked before the array is touched).
+ * The current device must be the one that owns `stream` and the pointers.
+ * The first call on a device looks up that device's copy of the array (make
+ * it before any stream capture); no call allocates.  All calls share the one
+ * array and each call clears the part that must start at zero, so calls
+ * whose GPU work overlaps (other streams, other host threads) race and must
+ * be serialised by the caller.  A device-side wait that gives up is recorded
+ * in the array and kept until mogt_gated_scan_fwd_noalloc_status reads it. */
 int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const void* v, const float* f,
                                 void* o, const float* S0, float* S_final, float* decay_final,
                                 void* chunk_states, int64_t BH, int64_t T, int64_t dk, int64_t dv,
                                 int in_dtype, int out_dtype, void* stream);
+
+/* Status of the allocation-free entry point on the current device: waits for
+ * `stream`, then *err_out = MOGT_OK or MOGT_ERR_TIMEOUT (the first failure
+ * since the last read) and *unit_out = the unit that recorded it; the record
+ * is cleared by the read.  No counterpart in the reference. */
+int mogt_gated_scan_fwd_noalloc_status(void* stream, int* err_out, uint32_t* unit_out);
 
 /* ---------------------------------------------------------------------------
  * Headed gated scan, backward: gradients of L = sum_t <o_t, do_t>.

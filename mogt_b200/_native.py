@@ -31,6 +31,7 @@ SIGNATURES = {
     "mogt_gated_scan_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
     "mogt_gated_scan_fwd": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp, _sz, _vp]),
     "mogt_gated_scan_fwd_noalloc": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp]),
+    "mogt_gated_scan_fwd_noalloc_status": (_int, [_vp, ctypes.POINTER(_int), ctypes.POINTER(ctypes.c_uint32)]),
     "mogt_gated_scan_bwd_workspace_bytes": (_sz, [_i64] * 4 + [_int]),
     "mogt_gated_scan_bwd": (_int, [_vp] * 12 + [_i64] * 4 + [_int, _vp, _sz, _vp]),
     "mogt_matrix_scan_fwd": (_int, [_vp] * 8 + [_i64] * 3 + [_int, _int, _vp]),
@@ -93,36 +94,124 @@ def stream_ptr(device) -> ctypes.c_void_p:
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
 
 
+# Device-side failures.  A look-back or mbarrier wait that gives up records
+# MOGT_ERR_TIMEOUT in the 256-byte header of the call's workspace (the kernel
+# then finishes with wrong results instead of hanging).  After every launch
+# the ops below queue a 4-byte copy of that word into pinned host memory; the
+# next call that uses the same workspace raises RuntimeError when the copy has
+# landed and shows an error, so a failure surfaces without a host
+# synchronisation on the hot path.  With MOGT_SYNC_CHECK=1 in the environment
+# every call waits for its own result and raises at once; check_errors()
+# waits and raises on demand.
+import os
+
+SYNC_CHECK = os.environ.get("MOGT_SYNC_CHECK", "0") not in ("", "0")
+
+
+class DeviceTimeout(RuntimeError):
+    """A bounded device-side wait gave up: the call's results are not valid."""
+
+
+def _raise_timeout(what, unit):
+    raise DeviceTimeout(f"{what}: a device-side wait timed out (unit {unit}); "
+                        "the results of that call are not valid")
+
+
+class _Workspace:
+    __slots__ = ("buf", "slot", "event", "what")
+
+    def __init__(self, buf):
+        self.buf = buf
+        self.slot = torch.zeros(2, dtype=torch.int32).pin_memory()
+        self.event = None
+        self.what = None
+
+    def clear_error(self):
+        self.buf[12:20].zero_()
+        self.slot.zero_()
+
+    def poll(self):
+        """Raise if an earlier call on this workspace recorded a timeout
+        whose status copy has already arrived (no synchronisation)."""
+        if self.event is not None and self.event.query():
+            self.event = None
+            err, unit = int(self.slot[0]), int(self.slot[1])
+            if err:
+                what = self.what
+                self.clear_error()
+                _raise_timeout(what, unit)
+
+    def after_launch(self, what):
+        self.what = what
+        stream = torch.cuda.current_stream(self.buf.device)
+        self.slot.copy_(self.buf[12:20].view(torch.int32), non_blocking=True)
+        if SYNC_CHECK:
+            stream.synchronize()
+            self.event = None
+            err, unit = int(self.slot[0]), int(self.slot[1])
+            if err:
+                self.clear_error()
+                _raise_timeout(what, unit)
+            return
+        ev = torch.cuda.Event()
+        ev.record(stream)
+        self.event = ev
+
+
 class _Workspaces:
-    """One zero-initialised workspace per (device, stream), grown on demand.
+    """One zero-initialised workspace per (device, stream, kernel family),
+    grown on demand.
 
     The kernels leave a workspace ready for the next call, so it is zeroed
     only when (re)allocated.  Calls on one stream are ordered, which is what
-    sharing a workspace requires."""
+    sharing a workspace requires.  Every kernel family has its own buffer:
+    their layouts differ, and a family that reused another's buffer could
+    read that family's state data as its flags."""
 
     def __init__(self):
         self._ws = {}
 
-    def get(self, device: torch.device, nbytes: int) -> torch.Tensor:
-        key = (device.index, torch.cuda.current_stream(device).cuda_stream)
-        buf = self._ws.get(key)
-        if buf is None or buf.numel() < nbytes:
-            size = max(nbytes, 0 if buf is None else int(buf.numel() * 1.5))
-            buf = torch.zeros(size + 256, dtype=torch.uint8, device=device)
-            self._ws[key] = buf
-        return buf
+    def entry(self, device: torch.device, nbytes: int, family: str) -> _Workspace:
+        key = (device.index, torch.cuda.current_stream(device).cuda_stream, family)
+        w = self._ws.get(key)
+        if w is None or w.buf.numel() < nbytes:
+            if w is not None:
+                w.poll()
+            size = max(nbytes, 0 if w is None else int(w.buf.numel() * 1.5))
+            w = _Workspace(torch.zeros(size + 256, dtype=torch.uint8, device=device))
+            self._ws[key] = w
+        else:
+            w.poll()
+        return w
+
+    def get(self, device: torch.device, nbytes: int, family: str = "misc") -> torch.Tensor:
+        return self.entry(device, nbytes, family).buf
 
     def status(self, device: torch.device):
         """(err, unit) of every workspace on `device` (synchronises)."""
         out = []
-        for (idx, s), buf in self._ws.items():
+        for (idx, s, _fam), w in self._ws.items():
             if idx != device.index:
                 continue
             err, unit = ctypes.c_int(0), ctypes.c_uint32(0)
-            check(lib().mogt_workspace_status(ptr(buf), ctypes.c_void_p(s), ctypes.byref(err),
+            check(lib().mogt_workspace_status(ptr(w.buf), ctypes.c_void_p(s), ctypes.byref(err),
                                               ctypes.byref(unit)), "mogt_workspace_status")
             out.append((err.value, unit.value))
         return out
+
+    def check(self, device: torch.device):
+        """Synchronise and raise DeviceTimeout if any workspace on `device`
+        holds a recorded timeout (the record is cleared)."""
+        torch.cuda.synchronize(device)
+        for (idx, _s, _fam), w in self._ws.items():
+            if idx != device.index:
+                continue
+            w.event = None
+            err, unit = (int(x) for x in w.buf[12:20].view(torch.int32).tolist())
+            if err:
+                what = w.what or "mogt kernel"
+                w.clear_error()
+                _raise_timeout(what, unit)
 
 
 workspaces = _Workspaces()
@@ -133,3 +222,10 @@ def workspace_errors(device=None):
     workspaces on `device` (0 = none).  Synchronises the device."""
     device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
     return [e for e, _ in workspaces.status(device)]
+
+
+def check_errors(device=None):
+    """Wait for `device` and raise DeviceTimeout if a call recorded a
+    device-side timeout since the last check."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    workspaces.check(device)

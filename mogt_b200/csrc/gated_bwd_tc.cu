@@ -39,7 +39,6 @@
 #include "common.cuh"
 #include "gated_common.cuh"
 #include "lookback.cuh"
-#include "trace.cuh"
 
 namespace mogt {
 namespace gated {
@@ -176,7 +175,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const float* fh = p.f + (size_t)bh * T;
   uint32_t ph_a = 0, ph_b = 0, ph_c = 0, ph_d = 0, ph_e = 0;
   bool ok = true;
-  MOGT_MARK(unit, 0);
 
   uint64_t pol_keep = 0, pol_stream = 0;
   if (tid == 0) {
@@ -309,7 +307,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (tid == 0)
       for (int it = n1; it < n1 + STAGES - 1; ++it) issue(it);
   }
-  MOGT_MARK(unit, 1);
   const float A_agg = fast_exp2(ltot);
   const size_t st_off = (size_t)unit * (D * D) + (size_t)tid * 16;
   if (n1 > 0 && ci > 0) {
@@ -333,7 +330,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                              reinterpret_cast<float*>(smem + SM_MISC + 64),
                              reinterpret_cast<volatile uint32_t*>(smem + SM_MISC + 16));
   }
-  MOGT_MARK(unit, 2);
   if (n1 > 0) {
     float4* dst = reinterpret_cast<float4*>(p.st_inc + st_off);
 #pragma unroll
@@ -346,7 +342,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     if (tid == 0) st_release_u32(p.flags + unit, flag_tag(epoch, kFlagInc));
   }
 
-  MOGT_MARK(unit, 3);
   // ---------------- pass 2: chunks in reverse ----------------
   // df of chunk gc from the partials of parity par: one warp, lane l owns
   // steps 2l and 2l+1
@@ -441,7 +436,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     const int gc = gl - j;
     const int slot = j % STAGES;
     const uint8_t* base = smem + SM_RING + slot * SLOT;
-    MOGT_CLK(unit, 5, j == 5);
     const WGates gt = warp_gates(fnext, lane);
     if (j + 1 < nc) fnext = gate_load(fh, T, gc - 1, lane);
     if (warp == 0) {
@@ -449,7 +443,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       *reinterpret_cast<float2*>(sgw + 2 * lane) = make_float2(gt.w0, gt.w1);
     }
     if (!mbar_wait(&bars[slot], (j / STAGES) & 1)) ok = false;
-    MOGT_CLK(unit, 6, j == 5);
     {
       const float e0 = fast_exp2(gt.l0), e1 = fast_exp2(gt.l1);
       build_rows(qh_tile, base + T_Q * TILE, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
@@ -461,7 +454,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_before();
     if (tid == 0) bulk_wait_read<0>();   // the previous chunk's dq, dk, dv stores have read their tiles
     __syncthreads();
-    MOGT_CLK(unit, 7, j == 5);
     // group 1: products of the raw tiles and the carry
     {
       const uint32_t qb = smem_u32(base + T_Q * TILE), kb = smem_u32(base + T_K * TILE),
@@ -508,7 +500,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tmem_ld_16x32_async(r_m, tw + TM_M1);
       tmem_ld_16x32_async(r_p, tw + TM_PQ);
       tmem_wait_ld();
-      MOGT_CLK(unit, 8, j == 5);
       float m1[4][4], pq[4][4], E[4][4];
       frag_from_u32(m1, r_m);
       frag_from_u32(pq, r_p);
@@ -587,11 +578,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         }
       }
     }
-    MOGT_CLK(unit, 9, j == 5);
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
-    MOGT_CLK(unit, 10, j == 5);
     // group 2: the masked products
     {
       const uint32_t qb = smem_u32(base + T_Q * TILE), db = smem_u32(base + T_DO * TILE);
@@ -625,7 +614,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       load_frag_bf16(qf, base + T_Q * TILE, fr);
       load_frag_bf16(kf, base + T_K * TILE, fr);
       tmem_wait_ld();
-      MOGT_CLK(unit, 11, j == 5);
       float dx[4][4];
       frag_from_u32(dos, r_dos);
       frag_from_u32(dx, r_dx);
@@ -648,7 +636,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tmem_ld_16x32_async(r_k2, tw + TM_DK2);
       tmem_ld_16x32_async(r_v2, tw + TM_DV2);
       tmem_wait_ld();
-      MOGT_CLK(unit, 12, j == 5);
       float q2[4][4], k2[4][4], v2[4][4];
       frag_from_u32(q2, r_q2);
       frag_from_u32(k2, r_k2);
@@ -698,7 +685,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       for (int o = 16; o > 0; o >>= 1) sg += __shfl_xor_sync(0xffffffffu, sg, o);
       if (lane == 0) part(SM_SIG, j & 1)[warp] = sg;
     }
-    MOGT_CLK(unit, 13, j == 5);
     tc_fence_before();
     __syncthreads();
     if (tid == 0) {
@@ -707,11 +693,9 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       tma_store_3d(&tdv, smem + SM_OUT + 2 * TILE, 0, gc * CH, bh);
       bulk_commit();
     }
-    MOGT_CLK(unit, 14, j == 5);
     gprev = gt;
   }
   if (warp == NTHREADS / 32 - 1 && nc > 0) compute_df(c_begin, gprev, (nc - 1) & 1);
-  MOGT_MARK(unit, 4);
   if (stripe == 0 && p.dS0) store_frag_rowmajor(p.dS0 + (size_t)bh * D * D, X, fr);
   if (tid == 0) bulk_wait<0>();
   if (!ok) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
@@ -731,9 +715,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 using namespace mogt;
 using namespace mogt::gated;
 
-#ifdef MOGT_TRACE
-extern "C" int mogt_debug_set_trace_bwd(void* buf) { return mogt::set_trace(buf); }
-#endif
 
 namespace mogt {
 namespace gated {

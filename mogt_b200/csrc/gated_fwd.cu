@@ -37,7 +37,6 @@
 #include "gated_internal.h"
 #include "lookback.cuh"
 
-#include "trace.cuh"
 
 namespace mogt {
 namespace gated {
@@ -139,7 +138,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
   const float* fh = p.f + (size_t)bh * T;
   uint32_t ph_m1 = 0, ph_m2 = 0, ph_m3 = 0;
   bool ok = true;
-  MOGT_MARK(unit, 0);
 
   uint64_t pol_keep = 0, pol_stream = 0;
   if (tid == 0) {
@@ -247,7 +245,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
     tc_fence_before();
     ltot = __uint_as_float(bc[2]);
   }
-  MOGT_MARK(unit, 1);
   if (n1 > 0) {
     // pass 1 has released the shared ring: prefetch the first pass-2 chunks so
     // they load during the look-back
@@ -286,7 +283,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                              reinterpret_cast<float*>(smem + SM_MISC + 64),
                              reinterpret_cast<volatile uint32_t*>(smem + SM_MISC + 16));
   }
-  MOGT_MARK(unit, 2);
 
   if (n1 > 0) {
     float inc_st[4][4];
@@ -308,7 +304,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       if (tid == 0 && p.decay_final) p.decay_final[bh] = A_agg * a_in;
     }
   }
-  MOGT_MARK(unit, 3);
 
   // ---------------- pass 2: outputs ----------------
   // Software pipeline, one CTA barrier per chunk.  In iteration c:
@@ -403,7 +398,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         gnext = warp_gates(fnext, lane);
         if (c + 2 < nc) fnext = gate_load(fh, T, gc0 + c + 2, lane);
       }
-      MOGT_CLK(unit, 5, c == 5);
       wait_bar(bar_m1, ph_m1);
       ph_m1 ^= 1u;
       wait_bar(bar_m3, ph_m3);
@@ -413,14 +407,12 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         ph_m2 ^= 1u;
       }
       tc_fence_after();
-      MOGT_CLK(unit, 6, c == 5);
       // the P and dS accumulators are read together
       const bool need_ds = c + 1 < nc || (final_here && p.S_final);
       uint32_t r_ds[16], r_p[16], r_o[16];
       if (need_ds) tmem_ld_16x32_async(r_ds, tw + TM_DS);
       if (want_out) tmem_ld_16x32_async(r_p, tw + TM_P);
       tmem_wait_ld();
-      MOGT_CLK(unit, 14, c == 5);
       // state for chunk c+1 (or the final state)
       const float dC = fast_exp2(gcur.tot);
       ltot2 += gcur.tot;
@@ -444,7 +436,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
             store_frag_rowmajor_bf16(p.chunk_states + ((size_t)bh * p.nchunks + gc0 + c + 1) * D * D, sin, fr);
         }
       }
-      MOGT_CLK(unit, 15, c == 5);
       // output of the previous chunk, read back only now: with all three
       // accumulators in flight at once the kernel spills at its 128-register cap
       if (want_out && c > 0) {
@@ -452,7 +443,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         tmem_wait_ld();
         write_out_regs(c - 1, r_o);
       }
-      MOGT_CLK(unit, 7, c == 5);
       // P'_c: causal mask (and the exact decays when they do not factorise)
       if (want_out) {
         float pacc[4][4];
@@ -481,17 +471,14 @@ __global__ void __launch_bounds__(NTHREADS, 2)
         }
         store_frag_bf16(pt_tile, pacc, fr);
       }
-      MOGT_CLK(unit, 8, c == 5);
       // operands of chunk c+1
       if (c + 1 < nc) {
         if (!mbar_wait(&bars[(c + 1) % STAGES], ((c + 1) / STAGES) & 1)) ok = false;
         build_chunk(c + 1, gnext);
       }
-      MOGT_CLK(unit, 9, c == 5);
       fence_proxy_async();
       tc_fence_before();
       __syncthreads();
-      MOGT_CLK(unit, 10, c == 5);
       if (tid == 0) {
         tc_fence_after();
         if (want_out) {
@@ -499,14 +486,11 @@ __global__ void __launch_bounds__(NTHREADS, 2)
           umma_64x64x64(tbase + TM_O0 + 64u * (c & 1), smem_u32(pt_tile), false, vb, true, true);
         }
         umma_commit(bar_m2);
-        MOGT_CLK(unit, 12, c == 5);
       }
       if (c + 1 < nc) issue_mma1(c + 1, factorises(gnext));
       if (warp == 3 && lane == 0) issue(it + STAGES - 1);  // chunk c+2 into chunk c-1's slot
       __syncwarp();
-      MOGT_CLK(unit, 13, c == 5);
       gcur = gnext;
-      MOGT_CLK(unit, 11, c == 5);
     }
     // output of the last chunk
     wait_bar(bar_m2, ph_m2);
@@ -523,7 +507,6 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       if (tid == 0 && p.decay_final) p.decay_final[bh] = a_in * fast_exp2(ltot2);
     }
   }
-  MOGT_MARK(unit, 4);
   if (!ok) record_error(p.hdr, MOGT_ERR_TIMEOUT, unit);
   tc_fence_before();
   __syncthreads();
@@ -546,9 +529,6 @@ static bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 
 extern "C" {
 
-#ifdef MOGT_TRACE
-int mogt_debug_set_trace(void* buf) { return mogt::set_trace(buf); }
-#endif
 
 int64_t mogt_gated_scan_num_chunks(int64_t T, int64_t dk, int64_t dv, int in_dtype) {
   if (in_dtype != MOGT_DTYPE_BF16 || dk != D || dv != D || T <= 0) return 0;
@@ -562,16 +542,50 @@ size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
   return ws_layout((size_t)BH * make_plan(BH, T, 2 * sm_count()).nstripes).total;
 }
 
+// Checks every argument of a bf16 forward call and, when it is valid, returns
+// the stripe plan and the workspace layout it needs.  Touches no memory.
+static int validate_bf16_fwd(const void* q, const void* k, const void* v, const float* f,
+                             const void* o, int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                             int out_dtype, Plan* pl, WsLayout* L) {
+  if (!k || !v || !f || (o && !q)) return MOGT_ERR_ARG;
+  if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
+  if (dk != D || dv != D) return MOGT_ERR_UNSUPPORTED;
+  if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+  if (!aligned16(k) || !aligned16(v) || (q && !aligned16(q)) || (o && !aligned16(o)))
+    return MOGT_ERR_ALIGN;
+  *pl = make_plan(BH, T, 2 * sm_count());
+  const size_t NU = (size_t)BH * pl->nstripes;
+  if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
+  *L = ws_layout(NU);
+  return MOGT_OK;
+}
+
+// The kernel's dynamic shared-memory limit is raised once per device.
+static int prepare_kernels() {
+  constexpr int kMaxDev = 64;
+  static bool done[kMaxDev] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return MOGT_ERR_LAUNCH;
+  if (dev < kMaxDev && done[dev]) return MOGT_OK;
+  if (cudaFuncSetAttribute(gated_fwd_stripe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SM_ALLOC) != cudaSuccess ||
+      cudaFuncSetAttribute(gated_fwd_stripe<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           SM_ALLOC) != cudaSuccess)
+    return MOGT_ERR_LAUNCH;
+  if (dev < kMaxDev) done[dev] = true;
+  return MOGT_OK;
+}
+
 int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
                         const float* S0, float* S_final, float* decay_final, void* chunk_states,
                         int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
                         void* workspace, size_t workspace_bytes, void* stream) {
   if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
   if (T == 0) return MOGT_OK;
-  if (!k || !v || !f || (o && !q)) return MOGT_ERR_ARG;
-  if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (in_dtype == MOGT_DTYPE_F32) {
+    if (!k || !v || !f || (o && !q)) return MOGT_ERR_ARG;
+    if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
     if (out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
     if (chunk_states) return MOGT_ERR_UNSUPPORTED;
     return launch_fwd_seq(static_cast<const float*>(q), static_cast<const float*>(k),
@@ -579,16 +593,14 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
                           decay_final, (int)BH, (int)T, (int)dk, (int)dv, s);
   }
   if (in_dtype != MOGT_DTYPE_BF16) return MOGT_ERR_DTYPE;
-  if (dk != D || dv != D) return MOGT_ERR_UNSUPPORTED;
-  if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
-  if (!aligned16(k) || !aligned16(v) || (q && !aligned16(q)) || (o && !aligned16(o)))
-    return MOGT_ERR_ALIGN;
-  const Plan pl = make_plan(BH, T, 2 * sm_count());
+  Plan pl;
+  WsLayout L;
+  const int vs = validate_bf16_fwd(q, k, v, f, o, BH, T, dk, dv, out_dtype, &pl, &L);
+  if (vs != MOGT_OK) return vs;
   const size_t NU = (size_t)BH * pl.nstripes;
-  if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
-  const WsLayout L = ws_layout(NU);
   if (!workspace || workspace_bytes < L.total) return MOGT_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOGT_ERR_ALIGN;
+  if (prepare_kernels() != MOGT_OK) return MOGT_ERR_LAUNCH;
 
   CUtensorMap maps[3];
   const void* srcs[3] = {q ? q : k, k, v};
@@ -620,13 +632,10 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   P.nchunks = pl.nchunks;
   P.cps = pl.cps;
   P.nstripes = pl.nstripes;
-  if (out_dtype == MOGT_DTYPE_F32) {
-    cudaFuncSetAttribute(gated_fwd_stripe<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC);
+  if (out_dtype == MOGT_DTYPE_F32)
     gated_fwd_stripe<true><<<(unsigned)NU, NTHREADS, SM_ALLOC, s>>>(maps[0], maps[1], maps[2], P);
-  } else {
-    cudaFuncSetAttribute(gated_fwd_stripe<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_ALLOC);
+  else
     gated_fwd_stripe<false><<<(unsigned)NU, NTHREADS, SM_ALLOC, s>>>(maps[0], maps[1], maps[2], P);
-  }
   return mogt_host::launch_status();
 }
 
@@ -637,6 +646,13 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
 // device image instead of a caller-provided workspace, for callers that
 // cannot allocate device memory.  The kernel and its arguments are exactly
 // those of mogt_gated_scan_fwd.
+//
+// The array starts as the zero-filled .bss of the module, which is a valid
+// look-back workspace; each call leaves the header (ticket, done counter,
+// epoch) ready for the next call and clears only the per-unit flag words,
+// because a call with another unit count lays its flags over words that an
+// earlier call filled with state data.  The sticky error word is never
+// cleared by a call: mogt_gated_scan_fwd_noalloc_status reads and clears it.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -673,19 +689,42 @@ extern "C" int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const v
                                            int in_dtype, int out_dtype, void* stream) {
   if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
   if (T == 0) return MOGT_OK;
-  size_t clear_bytes = 0;
-  if (in_dtype == MOGT_DTYPE_BF16 && dk == D && dv == D) {
-    if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
-    const Plan pl = make_plan(BH, T, 2 * sm_count());
-    const WsLayout L = ws_layout((size_t)BH * pl.nstripes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (in_dtype == MOGT_DTYPE_BF16) {
+    // every argument is checked before the shared array is touched
+    Plan pl;
+    WsLayout L;
+    const int vs = validate_bf16_fwd(q, k, v, f, o, BH, T, dk, dv, out_dtype, &pl, &L);
+    if (vs != MOGT_OK) return vs;
     if (L.total > kStaticScratchBytes) return MOGT_ERR_TOO_LARGE;
-    clear_bytes = L.st_agg;  // header, flags and decays must start at zero
+    uint8_t* scratch = static_cast<uint8_t*>(static_scratch_for_current_device());
+    if (!scratch) return MOGT_ERR_LAUNCH;
+    if (cudaMemsetAsync(scratch + L.flags, 0, L.a_agg - L.flags, s) != cudaSuccess)
+      return MOGT_ERR_LAUNCH;
+    return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk,
+                               dv, in_dtype, out_dtype, scratch, kStaticScratchBytes, stream);
   }
-  void* scratch = static_scratch_for_current_device();
+  // the fp32 path uses no scratch
+  return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk, dv,
+                             in_dtype, out_dtype, nullptr, 0, stream);
+}
+
+extern "C" int mogt_gated_scan_fwd_noalloc_status(void* stream, int* err_out, uint32_t* unit_out) {
+  if (!err_out) return MOGT_ERR_ARG;
+  uint8_t* scratch = static_cast<uint8_t*>(static_scratch_for_current_device());
   if (!scratch) return MOGT_ERR_LAUNCH;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (clear_bytes && cudaMemsetAsync(scratch, 0, clear_bytes, s) != cudaSuccess)
+  uint32_t h[5];
+  if (cudaMemcpyAsync(h, scratch, sizeof(h), cudaMemcpyDeviceToHost, s) != cudaSuccess ||
+      cudaStreamSynchronize(s) != cudaSuccess)
     return MOGT_ERR_LAUNCH;
-  return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk, dv,
-                             in_dtype, out_dtype, scratch, kStaticScratchBytes, stream);
+  *err_out = static_cast<int>(h[3]);
+  if (unit_out) *unit_out = h[4];
+  if (h[3] != 0) {
+    // read and clear: the next error is recorded afresh
+    if (cudaMemsetAsync(scratch + offsetof(WsHeader, err), 0, 2 * sizeof(uint32_t), s) != cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess)
+      return MOGT_ERR_LAUNCH;
+  }
+  return MOGT_OK;
 }

@@ -31,7 +31,6 @@
 // Kernel 3 (one CTA per head and chunk) forms o = o^loc + U S_in, U the
 // chunk's 64 x 64 matrix of u_t rows, and writes o in the output dtype.
 #include "common.cuh"
-#include "trace.cuh"
 
 namespace mogt {
 namespace mchunk {
@@ -542,9 +541,7 @@ __global__ void __launch_bounds__(NT, 2)
   int s = 0;
   for (; s < L; ++s) {
     const int sl = s & 1;
-    MOGT_CLK(item, 0, s == 10);
     if (!mbar_wait(&bar_a[sl], (s >> 1) & 1)) ok = false;
-    MOGT_CLK(item, 1, s == 10);
     // split A_t in place into Ah, and Al into its own tile (same layout)
     {
       float4* a4 = reinterpret_cast<float4*>(sm + OFF_A + sl * 16384);
@@ -561,7 +558,6 @@ __global__ void __launch_bounds__(NT, 2)
     fence_proxy_async();
     tc_fence_before();
     __syncthreads();
-    MOGT_CLK(item, 2, s == 10);
     if (tid == 0) {
       tc_fence_after();
       const uint32_t ya = smem_u32(sm + OFF_YH), yl = smem_u32(sm + OFF_YL);
@@ -585,15 +581,12 @@ __global__ void __launch_bounds__(NT, 2)
         umma_tf32(tbase + 128u, umma_desc_kmajor(yl + half * 16384) + sub, dah, true);  // cross term Yl Ah^T
       }
       umma_commit(bar_m);
-      MOGT_CLK(item, 3, s == 10);
       // A_{s+1} goes into the Al tile as soon as the products reading it are done
       if (mbar_wait(bar_lo, s & 1)) issue(s + 1);
       else ok = false;
-      MOGT_CLK(item, 4, s == 10);
     }
     if (!mbar_wait(bar_m, s & 1)) ok = false;
     tc_fence_after();
-    MOGT_CLK(item, 5, s == 10);
     {
       const uint32_t ta = tbase + ((uint32_t)(32 * lq) << 16) + 32u * hh;
       uint32_t r0[32];
@@ -610,7 +603,6 @@ __global__ void __launch_bounds__(NT, 2)
 #pragma unroll
       for (int j = 0; j < 32; ++j) x[j] += __uint_as_float(r0[j]);
     }
-    MOGT_CLK(item, 6, s == 10);
     const TI* kt = reinterpret_cast<const TI*>(sm + OFF_KQV + sl * 768);
     const TI* qt = kt + D;
     const TI* vt = qt + D;
@@ -650,11 +642,9 @@ __global__ void __launch_bounds__(NT, 2)
                         tf32_rna(x[4 * ch + 2] - hv.z), tf32_rna(x[4 * ch + 3] - hv.w));
       }
     }
-    MOGT_CLK(item, 7, s == 10);
     fence_proxy_async();
     tc_fence_before();
     ok = __syncthreads_and(ok);
-    MOGT_CLK(item, 8, s == 10);
     if (tid < 128) {
       const float sum = red[tid] + red[128 + tid];
       float* dst = tid < D ? u : o_loc;
@@ -769,6 +759,3 @@ extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const
   return mogt_host::launch_status();
 }
 
-#ifdef MOGT_TRACE
-extern "C" int mogt_debug_set_trace_matrix(void* buf) { return mogt::set_trace(buf); }
-#endif

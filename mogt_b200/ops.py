@@ -3,7 +3,10 @@
 Every function validates shapes the way the reference does (ValueError on bad
 rank/shape, triton_scan.py:193-201), refuses CPU tensors (the reference's
 Triton path raises the same way, triton_scan.py:191-192) and launches on the
-current CUDA stream.  Nothing here computes on the CPU.
+current CUDA stream.  Nothing here computes on the CPU.  A device-side wait
+that timed out in a call raises ``_native.DeviceTimeout`` from the next call
+that uses the same workspace (at once with MOGT_SYNC_CHECK=1), or from
+``mogt_b200.check_errors()``.
 """
 from __future__ import annotations
 
@@ -71,11 +74,13 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     icode, ocode = N.dtype_code(in_dtype), N.dtype_code(out_dtype)
     nbytes = L.mogt_gated_scan_fwd_workspace_bytes(BH, T, dk, dv, icode)
     with torch.cuda.device(dev):
-        ws = N.workspaces.get(dev, nbytes)
+        w = N.workspaces.entry(dev, nbytes, "gated_fwd")
+        ws = w.buf
         st = L.mogt_gated_scan_fwd(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o), N.ptr(S0),
                                    N.ptr(S_fin), N.ptr(dec), N.ptr(seg), BH, T, dk, dv, icode, ocode,
                                    N.ptr(ws), ws.numel(), N.stream_ptr(dev))
-    N.check(st, "mogt_gated_scan_fwd")
+        N.check(st, "mogt_gated_scan_fwd")
+        w.after_launch("mogt_gated_scan_fwd")
     return o, S_fin, dec, seg
 
 
@@ -118,14 +123,18 @@ def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False, chunk_
     code = N.dtype_code(dt)
     nbytes = L.mogt_gated_scan_bwd_workspace_bytes(B * H, T, dk, dv, code)
     with torch.cuda.device(dev):
+        w = None
         if dt == torch.bfloat16:
-            ws = N.workspaces.get(dev, nbytes)
+            w = N.workspaces.entry(dev, nbytes, "gated_bwd")
+            ws = w.buf
         else:
             ws = torch.empty(max(nbytes, 256), dtype=torch.uint8, device=dev)
         st = L.mogt_gated_scan_bwd(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(do), N.ptr(S0),
                                    N.ptr(cs), N.ptr(gq), N.ptr(gk), N.ptr(gv), N.ptr(gf), N.ptr(gS0),
                                    B * H, T, dk, dv, code, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
-    N.check(st, "mogt_gated_scan_bwd")
+        N.check(st, "mogt_gated_scan_bwd")
+        if w is not None:
+            w.after_launch("mogt_gated_scan_bwd")
     return gq, gk, gv, gf, gS0
 
 
@@ -172,11 +181,13 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
             return o, S_fin
         nbytes = L.mogt_matrix_scan_chunked_scratch_bytes(B * H, T, d)
         scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
-        status = N.workspaces.get(dev, 256)
+        w = N.workspaces.entry(dev, 256, "matrix_chunked")
+        status = w.buf
         st = L.mogt_matrix_scan_fwd_chunked(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
                                             N.ptr(S0), N.ptr(S_fin), B * H, T, d, icode, ocode,
                                             N.ptr(status), N.ptr(scratch), nbytes, N.stream_ptr(dev))
         N.check(st, "mogt_matrix_scan_fwd_chunked")
+        w.after_launch("mogt_matrix_scan_fwd_chunked")
     return o, S_fin
 
 
@@ -211,13 +222,15 @@ def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=No
     L_ = N.lib()
     nbytes = L_.mogt_diag_scan_norm_scratch_bytes(B, L, R, C, N.dtype_code(V.dtype))
     scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
-    status = N.workspaces.get(dev, 256)
     with torch.cuda.device(dev):
+        w = N.workspaces.entry(dev, 256, "diag_scan")
+        status = w.buf
         st = L_.mogt_diag_scan_norm_fwd(N.ptr(V), N.ptr(zz), zz.shape[-1], float(damping), N.ptr(H0),
                                         N.ptr(w), float(eps), N.ptr(y), N.ptr(Hf), B, L, R, C,
                                         N.dtype_code(V.dtype), N.dtype_code(out_dtype), N.ptr(status),
                                         N.ptr(scratch), scratch.numel(), N.stream_ptr(dev))
-    N.check(st, "mogt_diag_scan_norm_fwd")
+        N.check(st, "mogt_diag_scan_norm_fwd")
+        w.after_launch("mogt_diag_scan_norm_fwd")
     return y, Hf
 
 
@@ -253,13 +266,15 @@ def affine_scan(U, V, *, output_dtype=torch.float32, return_prefix=False, revers
     Lb = N.lib()
     nbytes = Lb.mogt_affine_scan_workspace_bytes(B, L, R, C)
     with torch.cuda.device(dev):
-        ws = N.workspaces.get(dev, nbytes)
+        w = N.workspaces.entry(dev, nbytes, "affine")
+        ws = w.buf
         st = Lb.mogt_affine_scan_fwd(N.ptr(U), N.ptr(V), N.ptr(H), N.ptr(P), B, L, R, C,
                                      N.dtype_code(U.dtype),
                                      N.dtype_code(V.dtype) if V is not None else N.dtype_code(U.dtype),
                                      N.dtype_code(output_dtype), int(reverse), N.ptr(ws), ws.numel(),
                                      N.stream_ptr(dev))
-    N.check(st, "mogt_affine_scan_fwd")
+        N.check(st, "mogt_affine_scan_fwd")
+        w.after_launch("mogt_affine_scan_fwd")
     return H, P
 
 

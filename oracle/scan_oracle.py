@@ -34,6 +34,8 @@ __all__ = [
     "gated_scan_backward",
     "matrix_scan",
     "matrix_scan_backward",
+    "matrix_scan_stream",
+    "matrix_scan_backward_stream",
 ]
 
 
@@ -224,7 +226,7 @@ def gated_scan(q, k, v, f, *, state_dtype=np.float64, S0=None, return_final=Fals
     for t in range(T):
         ft = ff[:, t][:, None, None]
         S = ft * S + (1.0 - ft) * (kf[:, t, :, None] * vf[:, t, None, :])
-        o[:, t] = np.einsum("nkv,nk->nv", S, qf[:, t])
+        o[:, t] = np.matmul(qf[:, t, None, :], S)[:, 0]
     o = o.reshape(B, Hh, T, dv)
     if return_final:
         return o, S.reshape(B, Hh, dk, dv)
@@ -252,7 +254,7 @@ def gated_scan_backward(q, k, v, f, do, *, state_dtype=np.float64):
         ft = ff[:, t][:, None, None]
         S = ft * S + (1.0 - ft) * (kf[:, t, :, None] * vf[:, t, None, :])
         S_all[:, t + 1] = S
-    dq = np.einsum("ntkv,ntv->ntk", S_all[:, 1:], dof)
+    dq = np.matmul(S_all[:, 1:], dof[..., None])[..., 0]
     dk_ = np.empty_like(kf)
     dv_ = np.empty_like(vf)
     df = np.empty_like(ff)
@@ -260,10 +262,11 @@ def gated_scan_backward(q, k, v, f, do, *, state_dtype=np.float64):
     for t in range(T - 1, -1, -1):
         sig = qf[:, t, :, None] * dof[:, t, None, :] + carry
         w = (1.0 - ff[:, t])[:, None]
-        dk_[:, t] = w * np.einsum("nkv,nv->nk", sig, vf[:, t])
-        dv_[:, t] = w * np.einsum("nkv,nk->nv", sig, kf[:, t])
-        kv = kf[:, t, :, None] * vf[:, t, None, :]
-        df[:, t] = np.einsum("nkv,nkv->n", sig, S_all[:, t]) - np.einsum("nkv,nkv->n", sig, kv)
+        sv = np.matmul(sig, vf[:, t, :, None])[..., 0]          # Sigma_t v_t
+        dk_[:, t] = w * sv
+        dv_[:, t] = w * np.matmul(kf[:, t, None, :], sig)[:, 0]  # Sigma_t^T k_t
+        # <Sigma, S_{t-1}> - <Sigma, k v^T> = <Sigma, S_{t-1}> - k . (Sigma v)
+        df[:, t] = (sig * S_all[:, t]).sum((1, 2)) - (kf[:, t] * sv).sum(1)
         carry = ff[:, t][:, None, None] * sig
     r = lambda x: x.reshape((B, Hh) + x.shape[1:])
     return r(dq), r(dk_), r(dv_), r(df)
@@ -304,3 +307,85 @@ def matrix_scan_backward(A, q, k, v, f, do, *, state_dtype=np.float64):
     df = -np.einsum("ntkv,ntkv->nt", gV, kv)
     r = lambda x: x.reshape((B, Hh) + x.shape[1:])
     return r(gU), r(dq), r(dk_), r(dv_), r(df)
+
+
+# --------------------------------------------------------------------------
+# Streaming forms of the dense-transition scan for full-size parity checks:
+# the same recurrence as affine_scan_sequential (affine_scan.py:14-62) and its
+# backward (affine_scan.py:65-124), stepped one t at a time so that no
+# [N, T, d, d] state history is materialised (config 3 would need 4.3 GB of
+# float64 states).  Inputs may be float32; every step runs in state_dtype.
+# --------------------------------------------------------------------------
+
+def matrix_scan_stream(A, q, k, v, f, *, state_dtype=np.float64, S0=None, return_final=False):
+    """o_t = S_t^T q_t with S_t = A_t S_{t-1} + (1-f_t) k_t v_t^T
+    (affine_scan.py:47-55's loop body with U = A, V = (1-f) k v^T).
+    A: [B,H,T,dk,dk]; q, k: [B,H,T,dk]; v: [B,H,T,dv]; f: [B,H,T]."""
+    B, Hh, T, dk = q.shape
+    dv = v.shape[-1]
+    Af, qf, kf, vf, ff = (_fold(x) for x in (A, q, k, v, f))
+    N = B * Hh
+    S = np.zeros((N, dk, dv), state_dtype) if S0 is None else _fold(S0).astype(state_dtype).copy()
+    o = np.empty((N, T, dv), state_dtype)
+    for t in range(T):
+        w = (1.0 - ff[:, t].astype(state_dtype))[:, None, None]
+        S = np.matmul(Af[:, t].astype(state_dtype), S) + w * (
+            kf[:, t, :, None].astype(state_dtype) * vf[:, t, None, :].astype(state_dtype))
+        o[:, t] = np.einsum("nkv,nk->nv", S, qf[:, t].astype(state_dtype))
+    o = o.reshape(B, Hh, T, dv)
+    if return_final:
+        return o, S.reshape(B, Hh, dk, dv)
+    return o
+
+
+def matrix_scan_backward_stream(A, q, k, v, f, do, *, state_dtype=np.float64, S0=None,
+                                chunk=64):
+    """Gradients of sum(o * do) for :func:`matrix_scan_stream`, the chain rule
+    through affine_scan.py:65-124 (Sigma_t = g_t + A_{t+1}^T Sigma_{t+1},
+    dA_t = Sigma_t S_{t-1}^T) with g_t = q_t do_t^T and V = (1-f) k v^T.
+    States are checkpointed every `chunk` steps and recomputed inside a chunk
+    during the reverse sweep.  Returns dA (float32), dq, dk, dv, df and dS0."""
+    B, Hh, T, dk = q.shape
+    dv = v.shape[-1]
+    Af, qf, kf, vf, ff, dof = (_fold(x) for x in (A, q, k, v, f, do))
+    N = B * Hh
+    sd = state_dtype
+    S = np.zeros((N, dk, dv), sd) if S0 is None else _fold(S0).astype(sd).copy()
+    nchk = (T + chunk - 1) // chunk
+    ck = np.empty((nchk, N, dk, dv), sd)
+
+    def step(S, t):
+        w = (1.0 - ff[:, t].astype(sd))[:, None, None]
+        return np.matmul(Af[:, t].astype(sd), S) + w * (
+            kf[:, t, :, None].astype(sd) * vf[:, t, None, :].astype(sd))
+
+    for t in range(T):
+        if t % chunk == 0:
+            ck[t // chunk] = S
+        S = step(S, t)
+    dA = np.empty(Af.shape, np.float32)
+    dq = np.empty((N, T, dk), sd)
+    dk_ = np.empty((N, T, dk), sd)
+    dv_ = np.empty((N, T, dv), sd)
+    df = np.empty((N, T), sd)
+    carry = np.zeros((N, dk, dv), sd)    # A_{t+1}^T Sigma_{t+1}
+    for c in range(nchk - 1, -1, -1):
+        t0, t1 = c * chunk, min(T, (c + 1) * chunk)
+        hist = np.empty((t1 - t0 + 1, N, dk, dv), sd)   # S_{t0-1} .. S_{t1-1}
+        hist[0] = ck[c]
+        for t in range(t0, t1):
+            hist[t - t0 + 1] = step(hist[t - t0], t)
+        for t in range(t1 - 1, t0 - 1, -1):
+            St, Sp = hist[t - t0 + 1], hist[t - t0]
+            qt, dot = qf[:, t].astype(sd), dof[:, t].astype(sd)
+            kt, vt = kf[:, t].astype(sd), vf[:, t].astype(sd)
+            dq[:, t] = np.einsum("nkv,nv->nk", St, dot)
+            sig = qt[:, :, None] * dot[:, None, :] + carry
+            dA[:, t] = np.matmul(sig, np.swapaxes(Sp, 1, 2))
+            w = (1.0 - ff[:, t].astype(sd))[:, None]
+            dk_[:, t] = w * np.einsum("nkv,nv->nk", sig, vt)
+            dv_[:, t] = w * np.einsum("nkv,nk->nv", sig, kt)
+            df[:, t] = -np.einsum("nkv,nk,nv->n", sig, kt, vt)
+            carry = np.matmul(np.swapaxes(Af[:, t].astype(sd), 1, 2), sig)
+    r = lambda x: x.reshape((B, Hh) + x.shape[1:])
+    return r(dA), r(dq), r(dk_), r(dv_), r(df), r(carry)

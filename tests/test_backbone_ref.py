@@ -1,6 +1,6 @@
 """The re-implemented MOGT backbone against the reference MOGTModel itself
-(model_mogt.py), CPU only: the reference tree is imported read-only from the
-build container and the test is skipped where it is absent.  Weights are
+(model_mogt.py), CPU only: the reference tree (MOGT_REFERENCE_DIR) is imported
+read-only and the test is skipped where it is absent.  Weights are
 copied from the reference model (same parameter names), the scan on both
 sides is the reference's sequential affine scan (affine_scan.py:14-62), so
 this pins the block and model plumbing around the scan."""
@@ -11,8 +11,9 @@ from pathlib import Path
 import pytest
 import torch
 
-REF = Path(os.environ.get("MOGT_REFERENCE_DIR", "/root/reference"))
-pytestmark = pytest.mark.skipif(not (REF / "model_mogt.py").exists(), reason="reference tree absent")
+REF = Path(os.environ["MOGT_REFERENCE_DIR"]) if os.environ.get("MOGT_REFERENCE_DIR") else None
+pytestmark = pytest.mark.skipif(REF is None or not (REF / "model_mogt.py").exists(),
+                                reason="reference tree absent (set MOGT_REFERENCE_DIR)")
 
 
 def _ref_modules():

@@ -116,3 +116,16 @@ def test_oracle_shape_errors():
         O.affine_scan_sequential(np.zeros((1, 2, 3, 3)), np.zeros((1, 2, 4, 3)))
     with pytest.raises(ValueError):
         O.affine_scan_sequential(np.zeros((2, 3, 3)), np.zeros((1, 2, 3, 3)))
+
+
+def test_streaming_matrix_forms_match_dense_oracle(golden):
+    """The streaming dense-transition forms used by the full-size checks equal
+    the dense composition (itself pinned to the reference's vectors)."""
+    d = golden("matrix_small_fp64")
+    A, q, k, v, f = (d[x] for x in ("A", "q", "k", "v", "f"))
+    o = O.matrix_scan_stream(A, q, k, v, f)
+    assert np.abs(o - d["o"]).max() <= 1e-10 * max(1.0, np.abs(d["o"]).max())
+    stream = O.matrix_scan_backward_stream(A, q, k, v, f, d["g"], chunk=7)
+    for name, b in zip(("dA", "dq", "dk", "dv", "df"), stream[:5]):
+        a = d[name]
+        assert np.abs(a - b).max() <= 1e-6 * np.abs(a).max(), name

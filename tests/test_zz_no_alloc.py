@@ -56,6 +56,11 @@ def test_noalloc_matches_workspace_entry_point_twice():
             errS = (S - S_ref).abs().max() / S_ref.abs().max()
             assert float(errS) <= TOL_BF16
             outs.append(o)
+            # no device-side wait gave up: the status reader says so
+            err, unit = ctypes.c_int(-1), ctypes.c_uint32(0)
+            assert L.mogt_gated_scan_fwd_noalloc_status(N.stream_ptr(dev), ctypes.byref(err),
+                                                        ctypes.byref(unit)) == 0
+            assert err.value == 0
     assert torch.isfinite(outs[-1].float()).all()
 
 
@@ -71,3 +76,7 @@ def test_noalloc_rejects_oversized_problems():
                                        N.stream_ptr(dev))
     assert st == N.ERR_TOO_LARGE
     assert b"16 MiB" in L.mogt_status_string(st)
+    # arguments are checked before the shared array is touched
+    st = L.mogt_gated_scan_fwd_noalloc(N.ptr(q), N.ptr(q), N.ptr(q), None, N.ptr(q), None, None,
+                                       None, None, 1, 64, 64, 64, N.BF16, N.BF16, N.stream_ptr(dev))
+    assert st == N.ERR_ARG
