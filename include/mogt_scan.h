@@ -31,7 +31,7 @@
 extern "C" {
 #endif
 
-#define MOGT_ABI_VERSION 1
+#define MOGT_ABI_VERSION 2
 
 enum mogt_status {
   MOGT_OK = 0,
@@ -153,8 +153,18 @@ int mogt_matrix_scan_fwd(const float* A, const void* q, const void* k, const voi
                          const float* f, void* o, const float* S0, float* S_final, int64_t BH,
                          int64_t T, int64_t d, int in_dtype, int out_dtype, void* stream);
 
+/* Arithmetic of the chunked dense-transition kernels. */
+enum mogt_matrix_mode {
+  MOGT_MATRIX_FP32 = 0,   /* fp32 FMAs, round-to-nearest (default) */
+  MOGT_MATRIX_TF32X3 = 1  /* tensor cores, three tf32 products per step (bf16
+                             q/k/v only); faster, but the tensor core's
+                             accumulation rounding is biased, so the error
+                             grows linearly with T for norm-preserving A
+                             (measured 4e-4 relative at T = 8192) */
+};
+
 /* Chunked form of mogt_matrix_scan_fwd for long sequences (d = 64 only),
- * with the same arguments, results and fp32 arithmetic plus:
+ * with the same arguments, results and arithmetic (see `mode`) plus:
  *   status  : a zero-initialised 256-byte workspace header (the one the
  *             gated-scan workspaces start with); a device-side wait that
  *             gives up records MOGT_ERR_TIMEOUT there
@@ -172,7 +182,33 @@ size_t mogt_matrix_scan_chunked_scratch_bytes(int64_t BH, int64_t T, int64_t d);
 int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const void* k, const void* v,
                                  const float* f, void* o, const float* S0, float* S_final,
                                  int64_t BH, int64_t T, int64_t d, int in_dtype, int out_dtype,
-                                 void* status, void* scratch, size_t scratch_bytes, void* stream);
+                                 int mode, void* status, void* scratch, size_t scratch_bytes,
+                                 void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Dense-transition headed scan, backward: gradients of L = sum_t <o_t, do_t>
+ * for mogt_matrix_scan_fwd_chunked (d = 64).  Replaces the reference's
+ * backward for this operator, affine_scan.py:65-124
+ * (affine_scan_sequential_backward on U = A, V = (1-f) k v^T; Sigma_t = g_t +
+ * A_{t+1}^T Sigma_{t+1}, dA_t = Sigma_t S_{t-1}^T) chained through the readout
+ * (g_t = q_t do_t^T).
+ *   A, q, k, v, f : the forward's inputs; d_o : [BH, T, d] (q's dtype);
+ *   saved   : the forward's `scratch` after that call (it holds each chunk's
+ *             entering state and transition product), unchanged since;
+ *   dA : [BH, T, d, d] fp32; dq, dk, dv : [BH, T, d] in the input dtype;
+ *   df : [BH, T] fp32; dS0 : [BH, d, d] fp32 gradient of the initial state,
+ *   or NULL;
+ *   status  : a zero-initialised 256-byte workspace header (timeouts);
+ *   scratch : >= mogt_matrix_scan_bwd_scratch_bytes(BH, T, d) bytes,
+ *             16-byte aligned, any contents.
+ * fp32 arithmetic (round-to-nearest FMAs) throughout; in_dtype bf16 or f32.
+ * ------------------------------------------------------------------------- */
+size_t mogt_matrix_scan_bwd_scratch_bytes(int64_t BH, int64_t T, int64_t d);
+int mogt_matrix_scan_bwd(const float* A, const void* q, const void* k, const void* v,
+                         const float* f, const void* d_o, const void* saved, float* dA, void* dq,
+                         void* dk, void* dv, float* df, float* dS0, int64_t BH, int64_t T, int64_t d,
+                         int in_dtype, void* status, void* scratch, size_t scratch_bytes,
+                         void* stream);
 
 /* ---------------------------------------------------------------------------
  * Diagonal gated scan with the RMSNorm readout fused: the MOGT block with the

@@ -5,20 +5,17 @@ Public API:
     name (triton_affine_scan_hybrid, triton_affine_local_scan,
     triton_fused_scan, _TritonAffineScanHybridAutograd);
   * ``gated_scan(q, k, v, f)``: the headed, gated form with autograd;
+  * ``matrix_scan(A, q, k, v, f)``: the dense-transition form with autograd;
+  * ``check_errors()``: raise if a kernel recorded a device-side timeout;
   * ``ops``: the tensor-level wrappers of the C ABI (include/mogt_scan.h).
 """
 from . import ops, triton_scan  # noqa: F401
 from .gated import gated_scan  # noqa: F401
+from .matrix import matrix_scan  # noqa: F401
+from ._native import check_errors  # noqa: F401
 
 
-def matrix_scan(A, q, k, v, f, *, initial_state=None, output_dtype=None):
-    """Dense-transition headed scan (forward): S_t = A_t S_{t-1} + (1-f_t) k_t v_t^T,
-    o_t = S_t^T q_t.  A: [B, H, T, d, d] fp32; q, k, v: [B, H, T, d]."""
-    o, _ = ops.matrix_scan_fwd(A, q, k, v, f, initial_state=initial_state, output_dtype=output_dtype)
-    return o
-
-
-__all__ = ["gated_scan", "matrix_scan", "ops", "triton_scan", "install_as_triton_scan"]
+__all__ = ["gated_scan", "matrix_scan", "check_errors", "ops", "triton_scan", "install_as_triton_scan"]
 
 
 def install_as_triton_scan():

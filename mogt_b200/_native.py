@@ -15,6 +15,7 @@ import torch
 LIB_PATH = Path(__file__).resolve().parent / "lib" / "libmogt_scan.so"
 
 F32, BF16, F16 = 0, 1, 2
+MATRIX_FP32, MATRIX_TF32X3 = 0, 1
 _DT = {torch.float32: F32, torch.bfloat16: BF16, torch.float16: F16}
 
 OK, ERR_SHAPE, ERR_DTYPE, ERR_ALIGN, ERR_LAUNCH, ERR_TIMEOUT, ERR_WORKSPACE, ERR_UNSUPPORTED, ERR_ARG, ERR_TOO_LARGE = range(10)
@@ -36,7 +37,9 @@ SIGNATURES = {
     "mogt_gated_scan_bwd": (_int, [_vp] * 12 + [_i64] * 4 + [_int, _vp, _sz, _vp]),
     "mogt_matrix_scan_fwd": (_int, [_vp] * 8 + [_i64] * 3 + [_int, _int, _vp]),
     "mogt_matrix_scan_chunked_scratch_bytes": (_sz, [_i64] * 3),
-    "mogt_matrix_scan_fwd_chunked": (_int, [_vp] * 8 + [_i64] * 3 + [_int, _int] + [_vp, _vp, _sz, _vp]),
+    "mogt_matrix_scan_fwd_chunked": (_int, [_vp] * 8 + [_i64] * 3 + [_int, _int, _int] + [_vp, _vp, _sz, _vp]),
+    "mogt_matrix_scan_bwd_scratch_bytes": (_sz, [_i64] * 3),
+    "mogt_matrix_scan_bwd": (_int, [_vp] * 13 + [_i64] * 3 + [_int, _vp, _vp, _sz, _vp]),
     "mogt_diag_scan_norm_scratch_bytes": (_sz, [_i64] * 4 + [_int]),
     "mogt_diag_scan_norm_fwd": (_int, [_vp, _vp, _i64, ctypes.c_float, _vp, _vp, ctypes.c_float, _vp, _vp]
                                 + [_i64] * 4 + [_int, _int, _vp, _vp, _sz, _vp]),
@@ -64,7 +67,7 @@ def lib():
                     fn = getattr(L, name)
                     fn.restype = res
                     fn.argtypes = args
-                if L.mogt_abi_version() != 1:
+                if L.mogt_abi_version() != 2:
                     raise RuntimeError("libmogt_scan.so ABI version mismatch")
                 _lib = L
     return _lib
@@ -178,7 +181,10 @@ class _Workspaces:
             if w is not None:
                 w.poll()
             size = max(nbytes, 0 if w is None else int(w.buf.numel() * 1.5))
-            w = _Workspace(torch.zeros(size + 256, dtype=torch.uint8, device=device))
+            # made outside inference mode: the buffers are updated in place by
+            # later calls whatever mode those run in
+            with torch.inference_mode(False):
+                w = _Workspace(torch.zeros(size + 256, dtype=torch.uint8, device=device))
             self._ws[key] = w
         else:
             w.poll()

@@ -713,7 +713,7 @@ extern "C" size_t mogt_matrix_scan_chunked_scratch_bytes(int64_t BH, int64_t T, 
 extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const void* k, const void* v,
                                             const float* f, void* o, const float* S0, float* S_final,
                                             int64_t BH, int64_t T, int64_t d, int in_dtype, int out_dtype,
-                                            void* status, void* scratch, size_t scratch_bytes,
+                                            int mode, void* status, void* scratch, size_t scratch_bytes,
                                             void* stream) {
   using namespace mogt::mchunk;
   if (BH <= 0 || T < 0) return MOGT_ERR_SHAPE;
@@ -731,6 +731,8 @@ extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const
   if (in_dtype != MOGT_DTYPE_BF16 && in_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
   if (out_dtype != MOGT_DTYPE_BF16 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
   if (in_dtype == MOGT_DTYPE_F32 && out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+  if (mode != MOGT_MATRIX_FP32 && mode != MOGT_MATRIX_TF32X3) return MOGT_ERR_ARG;
+  if (mode == MOGT_MATRIX_TF32X3 && in_dtype != MOGT_DTYPE_BF16) return MOGT_ERR_UNSUPPORTED;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   auto* hdr = static_cast<mogt::WsHeader*>(status);
   const size_t blk = (size_t)NB * D * D;
@@ -740,10 +742,13 @@ extern "C" int mogt_matrix_scan_fwd_chunked(const float* A, const void* q, const
   float* S_loc = P + blk;
   float* S_in = S_loc + blk;
   const int nb = (int)NB, Ti = (int)T, nc = (int)nch;
-  // bf16 inputs: the tensor-core (3xTF32) chunk kernel; fp32 inputs keep the
-  // fp32-FMA kernel
-  int rc = in_dtype == MOGT_DTYPE_BF16
+  // MOGT_MATRIX_FP32: fp32 FMAs (round-to-nearest, unbiased); MOGT_MATRIX_TF32X3:
+  // the tensor-core chunk kernel (bf16 q/k/v only), whose accumulation rounding
+  // is biased and drifts over long norm-preserving sequences
+  int rc = mode == MOGT_MATRIX_TF32X3
                ? launch_local_tc(A, q, k, v, f, o_loc, u, P, S_loc, (int)BH, nb, Ti, nc, hdr, st)
+           : in_dtype == MOGT_DTYPE_BF16
+               ? launch_local<__nv_bfloat16>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st)
                : launch_local<float>(A, q, k, v, f, o_loc, u, P, S_loc, nb, Ti, nc, hdr, st);
   if (rc != MOGT_OK) return rc;
   const size_t csmem = (size_t)CR * D * D * 4 + 2 * CC * SP * 4 + 8 * CR;

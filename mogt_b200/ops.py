@@ -14,7 +14,8 @@ import torch
 
 from . import _native as N
 
-__all__ = ["gated_scan_fwd", "gated_scan_bwd", "matrix_scan_fwd", "affine_scan", "affine_grad_u", "gated_num_chunks"]
+__all__ = ["gated_scan_fwd", "gated_scan_bwd", "matrix_scan_fwd", "matrix_scan_bwd", "diag_scan_norm",
+           "affine_scan", "affine_grad_u", "gated_num_chunks"]
 
 
 def _require_cuda(*ts, what):
@@ -139,17 +140,20 @@ def gated_scan_bwd(q, k, v, f, do, *, initial_state=None, want_dS0=False, chunk_
 
 
 def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False,
-                    chunked=None):
+                    chunked=None, precision="fp32", save_for_backward=False):
     """o_t = S_t^T q_t with S_t = A_t S_{t-1} + (1-f_t) k_t v_t^T (dense A_t).
     A: [B, H, T, d, d]; q, k, v: [B, H, T, d]; f: [B, H, T]; d in {16, 32, 64}.
-    Returns (o, S_final).
+    Returns (o, S_final), or (o, S_final, saved) with save_for_backward.
 
     d = 64 (the default for T > 64, `chunked=None`) runs the chunked kernels:
     every 64-step chunk's transition prefix products and local state in
-    parallel (bf16 q/k/v on the tensor cores with three tf32 products per
-    step, fp32 q/k/v with fp32 FMAs), the chunk carries composed per head,
-    then the outputs per chunk.
-    `chunked=False` forces the single sequential pass per head."""
+    parallel, the chunk carries composed per head, then the outputs per chunk.
+    `precision="fp32"` (default) computes the chunks with fp32 FMAs;
+    `"tf32x3"` on the tensor cores (bf16 q/k/v only), faster but with a bias
+    that grows with T (4e-4 relative at T = 8192 for Cayley transitions).
+    `chunked=False` forces the single sequential pass per head.
+    `save_for_backward=True` (chunked only) also returns the forward's
+    per-chunk states and products, which matrix_scan_bwd takes as `saved`."""
     _require_cuda(A, q, k, v, f, initial_state, what="matrix_scan")
     if A.ndim != 5 or q.ndim != 4:
         raise ValueError("A must be [B, H, T, d, d] and q, k, v [B, H, T, d]")
@@ -158,6 +162,8 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
         raise ValueError("A: [B, H, T, d, d]; q, k, v: [B, H, T, d]; f: [B, H, T]")
     if q.dtype not in (torch.bfloat16, torch.float32) or k.dtype != q.dtype or v.dtype != q.dtype:
         raise ValueError("q, k, v must share dtype bfloat16 or float32")
+    if precision not in ("fp32", "tf32x3"):
+        raise ValueError("precision must be 'fp32' or 'tf32x3'")
     out_dtype = output_dtype or q.dtype
     dev = q.device
     A = A.to(torch.float32).contiguous()
@@ -169,9 +175,12 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
     L = N.lib()
     icode, ocode = N.dtype_code(q.dtype), N.dtype_code(out_dtype)
     if chunked is None:
-        chunked = d == 64 and T > 64
+        chunked = d == 64 and (T > 64 or save_for_backward)
     if chunked and d != 64:
         raise ValueError("the chunked matrix scan supports d = 64 only")
+    if save_for_backward and not chunked:
+        raise ValueError("save_for_backward needs the chunked matrix scan (d = 64)")
+    mode = N.MATRIX_TF32X3 if precision == "tf32x3" else N.MATRIX_FP32
     with torch.cuda.device(dev):
         if not chunked:
             st = L.mogt_matrix_scan_fwd(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
@@ -182,13 +191,53 @@ def matrix_scan_fwd(A, q, k, v, f, *, initial_state=None, output_dtype=None, wan
         nbytes = L.mogt_matrix_scan_chunked_scratch_bytes(B * H, T, d)
         scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
         w = N.workspaces.entry(dev, 256, "matrix_chunked")
-        status = w.buf
         st = L.mogt_matrix_scan_fwd_chunked(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o),
-                                            N.ptr(S0), N.ptr(S_fin), B * H, T, d, icode, ocode,
-                                            N.ptr(status), N.ptr(scratch), nbytes, N.stream_ptr(dev))
+                                            N.ptr(S0), N.ptr(S_fin), B * H, T, d, icode, ocode, mode,
+                                            N.ptr(w.buf), N.ptr(scratch), nbytes, N.stream_ptr(dev))
         N.check(st, "mogt_matrix_scan_fwd_chunked")
         w.after_launch("mogt_matrix_scan_fwd_chunked")
+    if save_for_backward:
+        return o, S_fin, scratch
     return o, S_fin
+
+
+def matrix_scan_bwd(A, q, k, v, f, do, saved, *, want_dS0=False):
+    """Gradients of sum(o * do) for o = matrix_scan_fwd(A, q, k, v, f) (d = 64):
+    returns (dA fp32, dq, dk, dv in the input dtype, df fp32, dS0 fp32 or
+    None).  `saved` is the third result of matrix_scan_fwd(...,
+    save_for_backward=True) on the same inputs (initial state included)."""
+    _require_cuda(A, q, k, v, f, do, saved, what="matrix_scan backward")
+    B, H, T, d = q.shape
+    if A.shape != (B, H, T, d, d) or k.shape != q.shape or v.shape != q.shape or do.shape != q.shape \
+            or f.shape != (B, H, T):
+        raise ValueError("A: [B, H, T, d, d]; q, k, v, do: [B, H, T, d]; f: [B, H, T]")
+    if d != 64:
+        raise ValueError("the dense-transition backward supports d = 64")
+    dt = q.dtype
+    if dt not in (torch.bfloat16, torch.float32):
+        raise ValueError("q, k, v must be bfloat16 or float32")
+    dev = q.device
+    A = A.to(torch.float32).contiguous()
+    q, k, v, do = (t.to(dt).contiguous() for t in (q, k, v, do))
+    f = f.to(torch.float32).contiguous()
+    L = N.lib()
+    if saved.numel() < L.mogt_matrix_scan_chunked_scratch_bytes(B * H, T, d):
+        raise ValueError("`saved` is not the forward's saved state for these shapes")
+    dA = torch.empty(B, H, T, d, d, dtype=torch.float32, device=dev)
+    gq, gk, gv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    gf = torch.empty(B, H, T, dtype=torch.float32, device=dev)
+    gS0 = torch.empty(B, H, d, d, dtype=torch.float32, device=dev) if want_dS0 else None
+    nbytes = L.mogt_matrix_scan_bwd_scratch_bytes(B * H, T, d)
+    with torch.cuda.device(dev):
+        scratch = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+        w = N.workspaces.entry(dev, 256, "matrix_bwd")
+        st = L.mogt_matrix_scan_bwd(N.ptr(A), N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(do),
+                                    N.ptr(saved), N.ptr(dA), N.ptr(gq), N.ptr(gk), N.ptr(gv), N.ptr(gf),
+                                    N.ptr(gS0), B * H, T, d, N.dtype_code(dt), N.ptr(w.buf),
+                                    N.ptr(scratch), nbytes, N.stream_ptr(dev))
+        N.check(st, "mogt_matrix_scan_bwd")
+        w.after_launch("mogt_matrix_scan_bwd")
+    return dA, gq, gk, gv, gf, gS0
 
 
 def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=None,
@@ -223,14 +272,14 @@ def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=No
     nbytes = L_.mogt_diag_scan_norm_scratch_bytes(B, L, R, C, N.dtype_code(V.dtype))
     scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
     with torch.cuda.device(dev):
-        w = N.workspaces.entry(dev, 256, "diag_scan")
-        status = w.buf
+        wse = N.workspaces.entry(dev, 256, "diag_scan")
+        status = wse.buf
         st = L_.mogt_diag_scan_norm_fwd(N.ptr(V), N.ptr(zz), zz.shape[-1], float(damping), N.ptr(H0),
                                         N.ptr(w), float(eps), N.ptr(y), N.ptr(Hf), B, L, R, C,
                                         N.dtype_code(V.dtype), N.dtype_code(out_dtype), N.ptr(status),
                                         N.ptr(scratch), scratch.numel(), N.stream_ptr(dev))
         N.check(st, "mogt_diag_scan_norm_fwd")
-        w.after_launch("mogt_diag_scan_norm_fwd")
+        wse.after_launch("mogt_diag_scan_norm_fwd")
     return y, Hf
 
 

@@ -27,7 +27,7 @@ def test_library_exports_every_declared_symbol():
     for name in declared_symbols():
         assert hasattr(lib, name), name
     assert declared_symbols() == set(_native.SIGNATURES), "ctypes table out of sync with the header"
-    assert lib.mogt_abi_version() == 1
+    assert lib.mogt_abi_version() == 2
     assert lib.mogt_status_string(5) == b"device-side wait timed out"
 
 
