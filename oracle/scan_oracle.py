@@ -389,3 +389,31 @@ def matrix_scan_backward_stream(A, q, k, v, f, do, *, state_dtype=np.float64, S0
             carry = np.matmul(np.swapaxes(Af[:, t].astype(sd), 1, 2), sig)
     r = lambda x: x.reshape((B, Hh) + x.shape[1:])
     return r(dA), r(dq), r(dk_), r(dv_), r(df), r(carry)
+
+
+# --------------------------------------------------------------------------
+# Torch form of the reference's CPU path, for the timed CPU baseline: the
+# same per-step batched matmul loop affine_scan.py:47-55 runs (fp32 state,
+# dense f*I transitions, one bmm plus one add per step, the states stacked at
+# the end), followed by the readout einsum.  Timing this form measures the
+# reference's own CPU code path (torch ops on the host cores); the numpy
+# restatement above is the checker.
+# --------------------------------------------------------------------------
+
+def gated_scan_torch_reference_path(q, k, v, f):
+    """q, k, v: [B, H, T, d] float32 torch tensors, f: [B, H, T]; returns o."""
+    import torch
+    B, Hh, T, dk = q.shape
+    dv = v.shape[-1]
+    N = B * Hh
+    ff = f.reshape(N, T).float()
+    U = ff[..., None, None] * torch.eye(dk, dtype=torch.float32)
+    Vin = (1.0 - ff)[..., None, None] * (k.reshape(N, T, dk, 1).float() * v.reshape(N, T, 1, dv).float())
+    H = torch.zeros(N, dk, dv, dtype=torch.float32)
+    states = []
+    for t in range(T):
+        H = torch.bmm(U[:, t], H) + Vin[:, t]
+        states.append(H)
+    S = torch.stack(states, dim=1)
+    o = torch.einsum("ntkv,ntk->ntv", S, q.reshape(N, T, dk).float())
+    return o.reshape(B, Hh, T, dv)

@@ -129,3 +129,12 @@ def test_streaming_matrix_forms_match_dense_oracle(golden):
     for name, b in zip(("dA", "dq", "dk", "dv", "df"), stream[:5]):
         a = d[name]
         assert np.abs(a - b).max() <= 1e-6 * np.abs(a).max(), name
+
+
+def test_torch_reference_path_matches_oracle():
+    """The torch form timed as the CPU baseline computes the oracle's result."""
+    from tests.helpers import as64, headed_bf16
+    q, k, v, f = headed_bf16(1, 3, 130, seed=4)
+    o = O.gated_scan_torch_reference_path(q.float(), k.float(), v.float(), f)
+    r = O.gated_scan(*as64(q, k, v, f))
+    assert np.abs(o.numpy() - r).max() <= 1e-5 * np.abs(r).max()
