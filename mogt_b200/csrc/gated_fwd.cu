@@ -36,10 +36,6 @@
 #include "gated_common.cuh"
 #include "gated_internal.h"
 #include "lookback.cuh"
-#include "gated_fwd_ws.cuh"
-
-#include <cstdlib>
-#include <cstring>
 
 
 namespace mogt {
@@ -603,16 +599,8 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   if (vs != MOGT_OK) return vs;
   if (!workspace || workspace_bytes < L.total) return MOGT_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOGT_ERR_ALIGN;
-  // the warp-specialised kernel runs one CTA per SM: its stripe plan targets
-  // the SM count (fewer units than the workspace was sized for)
-  const char* sel = getenv("MOGT_FWD_KERNEL");
-  const bool use_ws = !(sel && sel[0] == 's');
-  if (use_ws) {
-    pl = make_plan(BH, T, sm_count());
-    L = ws_layout((size_t)BH * pl.nstripes);
-  }
   const size_t NU = (size_t)BH * pl.nstripes;
-  if (!use_ws && prepare_kernels() != MOGT_OK) return MOGT_ERR_LAUNCH;
+  if (prepare_kernels() != MOGT_OK) return MOGT_ERR_LAUNCH;
 
   CUtensorMap maps[3];
   const void* srcs[3] = {q ? q : k, k, v};
@@ -644,12 +632,6 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   P.nchunks = pl.nchunks;
   P.cps = pl.cps;
   P.nstripes = pl.nstripes;
-  if (use_ws) {
-    static_assert(sizeof(Params) == sizeof(ws::Params), "parameter blocks agree");
-    ws::Params W;
-    memcpy(&W, &P, sizeof(W));
-    return launch_fwd_ws(maps, &W, out_dtype == MOGT_DTYPE_F32, (unsigned)NU, s);
-  }
   if (out_dtype == MOGT_DTYPE_F32)
     gated_fwd_stripe<true><<<(unsigned)NU, NTHREADS, SM_ALLOC, s>>>(maps[0], maps[1], maps[2], P);
   else

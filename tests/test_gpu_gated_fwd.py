@@ -136,3 +136,23 @@ def test_errors(mg):
         m.gated_scan(q.cuda()[..., :32], k.cuda()[..., :32], v.cuda()[..., :32], f.cuda())
     with pytest.raises(ValueError):
         m.gated_scan(q.cuda(), k.cuda(), v.cuda(), f.cuda()[..., :8])
+
+
+@pytest.mark.parametrize("H,T", [(12, 3584), (12, 5000), (12, 6000), (1, 5000)])
+def test_every_output_row_written(mg, H, T):
+    """Outputs prefilled with NaN: every row of every stripe must be written
+    (stripes of 5 to 8 chunks at H = 12, one stripe per chunk at H = 1), and
+    must match the oracle."""
+    m, N = mg
+    q, k, v, f = headed_bf16(1, H, T, seed=21)
+    qc, kc, vc, fc = (t.cuda() for t in (q, k, v, f))
+    L = N.lib()
+    nb = L.mogt_gated_scan_fwd_workspace_bytes(H, T, 64, 64, N.BF16)
+    ws = torch.zeros(nb, dtype=torch.uint8, device="cuda")
+    o = torch.full((1, H, T, 64), float("nan"), dtype=torch.float32, device="cuda")
+    st = L.mogt_gated_scan_fwd(N.ptr(qc), N.ptr(kc), N.ptr(vc), N.ptr(fc), N.ptr(o), None, None, None, None,
+                               H, T, 64, 64, N.BF16, N.F32, N.ptr(ws), nb, N.stream_ptr(qc.device))
+    assert st == 0
+    assert torch.isfinite(o).all()
+    ref = O.gated_scan(*as64(q, k, v, f))
+    assert rel_max_err(o.cpu().numpy(), ref) <= TOL_BF16
