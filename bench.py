@@ -380,6 +380,7 @@ def run_b200(args):
             extra["backbone"] = bb
             extra["gated_bwd_config2"] = extra_backward(dev, B, H, T)
             extra["matrix_scan_config3"] = extra_matrix(dev)
+            extra["config2_sweep"] = extra_config2_sweep(dev)
             if sp is not None:
                 extra["sequence_parallel_config5"] = sp
 
@@ -514,38 +515,73 @@ def extra_sp(dev, world, rank):
             "note": "state-only segment scan + NCCL all-gather of (decay, state) carries + local scan"}
 
 
+def _time_call(call, n, warm=2):
+    import torch
+    for _ in range(warm):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
 def extra_matrix(dev):
     """dense Cayley transitions, B=2, H=8, T=8192, d=64,
-    bf16 q/k/v, fp32 A; minimal flops per (step, head) 2*64^3 + 2*64^2 + 2*64^2
-    = 540,672 and bytes 16,900 (A 16384 + q,k,v 384 + f 4 + o 128)."""
+    bf16 q/k/v, fp32 A.  Forward: minimal flops per (step, head) 2*64^3 +
+    2*64^2 + 2*64^2 = 540,672 and bytes 16,900 (A 16384 + q,k,v 384 + f 4 +
+    o 128).  Backward: bytes per (step, head) A 16384 read + dA 16384 written
+    + q,k,v,do,f read (516) + dq,dk,dv,df written (388) = 33,672; minimal
+    flops 3 * 2 * 64^3 (state recompute, adjoint carry, dA) = 1,572,864."""
     import torch
     from mogt_b200 import ops
     B, H, T, d = 2, 8, 8192, 64
-    g = torch.Generator(device=dev).manual_seed(11)
-    M = torch.randn(B, H, T, d, d, generator=g, device=dev)
-    W = 0.05 * (M - M.transpose(-1, -2))
-    I = torch.eye(d, device=dev)
-    A = torch.linalg.solve(I - W, I + W).contiguous()  # solve returns column-major batches
-    del M, W
+    A = _cayley_transitions(B, H, T, d, dev, 11)
+    g = torch.Generator(device=dev).manual_seed(12)
     q, k, v = (torch.randn(B, H, T, d, generator=g, device=dev).bfloat16() for _ in range(3))
     f = torch.sigmoid(torch.randn(B, H, T, generator=g, device=dev) + 2.0)
-    for _ in range(2):
-        ops.matrix_scan_fwd(A, q, k, v, f)
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    n = 3
-    e0.record()
-    for _ in range(n):
-        ops.matrix_scan_fwd(A, q, k, v, f)
-    e1.record()
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / n
     units = B * H * T
-    del A
+    out = {}
+    for prec in ("fp32", "tf32x3"):
+        ms = _time_call(lambda: ops.matrix_scan_fwd(A, q, k, v, f, precision=prec), 3)
+        out[f"fwd_{prec}"] = {"ms": ms, "TFLOPs": units * 540672 / (ms / 1e3) / 1e12,
+                              "GBps": units * 16900 / (ms / 1e3) / 1e9}
+    out["fwd_fp32"]["note"] = ("default: chunked, per-chunk [P | S_loc] with fp32 FMAs (round-to-nearest), "
+                               "carries per head, outputs per chunk; within 1e-5 of the fp64 oracle at T=8192")
+    out["fwd_tf32x3"]["note"] = ("opt-in tensor-core form (3xTF32 tcgen05); its accumulation bias reaches "
+                                 "4e-4 relative at T=8192, above the 1e-4 fp32 bar")
+    do = torch.randn(B, H, T, d, generator=g, device=dev).bfloat16()
+    _, _, saved = ops.matrix_scan_fwd(A, q, k, v, f, save_for_backward=True)
+    ms = _time_call(lambda: ops.matrix_scan_bwd(A, q, k, v, f, do, saved), 2, warm=1)
+    out["bwd"] = {"ms": ms, "TFLOPs": units * 1572864 / (ms / 1e3) / 1e12,
+                  "GBps": units * 33672 / (ms / 1e3) / 1e9,
+                  "note": "reverse-time chunked on the forward's saved chunk states, fp32 FMAs; "
+                          "includes the Python-side output allocation"}
+    del A, saved
     torch.cuda.empty_cache()
-    return {"ms": ms, "TFLOPs": units * 540672 / (ms / 1e3) / 1e12,
-            "GBps": units * 16900 / (ms / 1e3) / 1e9,
-            "note": "chunked: per-chunk [P | S_loc] evolved on tcgen05 tensor cores (3xTF32, fp32-level accuracy; 2x the minimal FLOP), carries per head, outputs per chunk; A is 2.2 GB > L2"}
+    return out
+
+
+def extra_config2_sweep(dev):
+    """BASELINE config 2 at T = 8192 and 16384 (the bench line is T = 32768):
+    forward and backward timed separately, 516 / 904 algorithmic bytes per
+    (token, head)."""
+    from mogt_b200 import ops
+    import torch
+    out = {}
+    for T in (8192, 16384):
+        q, k, v, f = (t.to(dev) for t in make_inputs(1, 12, T, 7000 + T))
+        g = torch.randn(1, 12, T, 64, generator=torch.Generator().manual_seed(T)).to(dev).bfloat16()
+        ms_f = _time_call(lambda: ops.gated_scan_fwd(q, k, v, f), 20)
+        _, _, _, cs = ops.gated_scan_fwd(q, k, v, f, save_states=True)
+        ms_b = _time_call(lambda: ops.gated_scan_bwd(q, k, v, f, g, chunk_states=cs), 20)
+        out[f"T{T}"] = {"fwd_ms": ms_f, "fwd_tokens_per_s": T / (ms_f / 1e3),
+                        "fwd_GBps": 516 * 12 * T / (ms_f / 1e3) / 1e9,
+                        "bwd_ms": ms_b, "bwd_GBps": 904 * 12 * T / (ms_b / 1e3) / 1e9}
+    return out
 
 
 def extra_backbone(dev, world, rank):
@@ -641,6 +677,30 @@ def _case_diag(B, L):
     return make
 
 
+def _case_matrix_bwd(B, H, T):
+    def make(dev):
+        import torch
+        from mogt_b200 import ops
+        A = _cayley_transitions(B, H, T, 64, dev, 11)
+        g = torch.Generator(device=dev).manual_seed(12)
+        q, k, v, do = (torch.randn(B, H, T, 64, generator=g, device=dev).bfloat16() for _ in range(4))
+        f = torch.sigmoid(torch.randn(B, H, T, generator=g, device=dev) + 2.0)
+        _, _, saved = ops.matrix_scan_fwd(A, q, k, v, f, save_for_backward=True)
+        return lambda: ops.matrix_scan_bwd(A, q, k, v, f, do, saved)
+    return make
+
+
+def _case_affine(B, L, C):
+    def make(dev):
+        import torch
+        from mogt_b200 import ops
+        g = torch.Generator().manual_seed(7)
+        U = (torch.eye(16) + 0.01 * torch.randn(B, L, 16, 16, generator=g)).to(dev)
+        V = torch.randn(B, L, 16, C, generator=g).to(dev)
+        return lambda: ops.affine_scan(U, V)
+    return make
+
+
 # name -> builder of a zero-argument call; each case runs the call three times
 PROFILE_CASES = {
     "fwd_config2": _case_fwd_config2,                 # gated forward, B=1 H=12 T=32768
@@ -649,6 +709,10 @@ PROFILE_CASES = {
     "matrix_small": _case_matrix(1, 16, 2048),        # 512 chunk CTAs, A = 537 MB
     "diag_backbone": _case_diag(8, 32768),            # fused diagonal scan + norm, backbone shape
     "diag_small": _case_diag(8, 16384),
+    "matrix_bwd_config3": _case_matrix_bwd(2, 8, 8192),  # dense-transition backward, A + dA = 4.3 GB
+    "matrix_bwd_small": _case_matrix_bwd(1, 16, 2048),
+    "affine_r16_c48": _case_affine(1, 32768, 48),        # reference-shape dense scan, 235 MB
+    "affine_backbone": _case_affine(8, 32768, 48),
 }
 
 
