@@ -238,6 +238,21 @@ int mogt_diag_scan_norm_fwd(const void* V, const float* z, int64_t z_per_token, 
                             size_t scratch_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Connection map of the MOGT block (replaces model_mogt.py:79-102,
+ * _build_transport: torch.matrix_exp / torch.linalg.solve on [B, L, r, r]).
+ * For each of `count` n x n matrices M (row-major, consecutive):
+ *   A = (M - M^T) * scale         (skew != 0; the block's antisymmetrised
+ *                                  phi_conn output, scale = 1 / r)
+ *   A = M                         (skew == 0)
+ *   U = damping * expm(A)                         mode MOGT_CONN_EXPM
+ *   U = damping * (I - A/2)^{-1} (I + A/2)        mode MOGT_CONN_CAYLEY
+ * fp32 arithmetic; M in_dtype, U out_dtype (f32 or bf16); n in {8, 16, 32}.
+ * ------------------------------------------------------------------------- */
+enum mogt_conn_mode { MOGT_CONN_EXPM = 0, MOGT_CONN_CAYLEY = 1 };
+int mogt_connection_map(const void* M, void* U, int64_t count, int64_t n, int mode, int skew,
+                        float scale, float damping, int in_dtype, int out_dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).
  * Replaces triton_scan.py:232-311 (_triton_affine_scan_hybrid_forward: local
  * Triton kernel + Python carry scan + carry apply), triton_scan.py:151-175

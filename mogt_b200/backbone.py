@@ -89,7 +89,13 @@ class MOGTBlock(nn.Module):
         damping = float(getattr(self, "connection_damping", 0.999))
         if impl == "identity":
             U = self._identity_r.view(1, 1, self.r, self.r).expand(B, L, self.r, self.r)
+        elif x_norm.is_cuda:
+            # on the GPU: the connection-map kernel (mogt_connection_map)
+            from .connection import connection_map
+            return connection_map(self.phi_conn(x_norm).view(B, L, self.r, self.r), impl, damping,
+                                  output_dtype=x_norm.dtype)
         else:
+            # CPU tensors (the parity harness against the reference model)
             A = self.phi_conn(x_norm).view(B, L, self.r, self.r)
             A = ((A - A.transpose(-2, -1)) / self.r).float()
             if impl == "matrix_exp":
