@@ -381,6 +381,7 @@ def run_b200(args):
             extra["gated_bwd_config2"] = extra_backward(dev, B, H, T)
             extra["matrix_scan_config3"] = extra_matrix(dev)
             extra["config2_sweep"] = extra_config2_sweep(dev)
+            extra["connection_map_backbone"] = extra_connection(dev)
             if sp is not None:
                 extra["sequence_parallel_config5"] = sp
 
@@ -562,6 +563,27 @@ def extra_matrix(dev):
                           "includes the Python-side output allocation"}
     del A, saved
     torch.cuda.empty_cache()
+    return out
+
+
+def extra_connection(dev):
+    """Connection map at the backbone shape (B=8, L=32768, r=16; one layer):
+    the kernel against torch.matrix_exp (what the reference calls,
+    model_mogt.py:85) on the same GPU.  Bytes per token: M bf16 512 + U bf16
+    512."""
+    import torch
+    from mogt_b200.connection import connection_map
+    g = torch.Generator(device=dev).manual_seed(3)
+    M = (0.05 * torch.randn(8, 32768, 16, 16, generator=g, device=dev)).bfloat16()
+    out = {}
+    for impl in ("matrix_exp", "cayley"):
+        ms = _time_call(lambda: connection_map(M, impl), 5)
+        out[impl] = {"ms": ms, "matrices_per_s": M.numel() / 256 / (ms / 1e3)}
+
+    def torch_expm():
+        A = (M - M.transpose(-1, -2)).float() / 16
+        return (torch.matrix_exp(A) * 0.999).to(M.dtype)
+    out["torch_matrix_exp_ms"] = _time_call(torch_expm, 3)
     return out
 
 

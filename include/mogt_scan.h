@@ -253,6 +253,23 @@ int mogt_connection_map(const void* M, void* U, int64_t count, int64_t n, int mo
                         float scale, float damping, int in_dtype, int out_dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Softmax cross-entropy rows of the chunked linear cross-entropy (replaces the
+ * F.cross_entropy / softmax steps of chunked_lm_loss.py:25-35, 52-61).
+ *   logits : [rows, V] fp32 (one chunk's hidden @ weight^T), 16-byte aligned
+ *            rows when V % 4 == 0 for the vector path;
+ *   labels : [rows] int64 in [0, V) or -100 (ignored by the loss);
+ *   fwd: lse[i] = log sum_j exp(logits[i, j]); loss[i] = lse[i] -
+ *        logits[i, labels[i]] (0 for -100);
+ *   bwd: in place, logits[i, j] = (exp(logits[i, j] - lse[i]) - [j == l_i]) *
+ *        scale with l_i = labels[i] (+ V when negative, as the reference's
+ *        indexing does).
+ * ------------------------------------------------------------------------- */
+int mogt_ce_rows_fwd(const float* logits, const int64_t* labels, int64_t rows, int64_t V, float* lse,
+                     float* loss, void* stream);
+int mogt_ce_rows_bwd(float* logits, const int64_t* labels, const float* lse, int64_t rows, int64_t V,
+                     float scale, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Dense affine scan H_t = U_t H_{t-1} + V_t, H_{-1} = 0 (fp32 state).
  * Replaces triton_scan.py:232-311 (_triton_affine_scan_hybrid_forward: local
  * Triton kernel + Python carry scan + carry apply), triton_scan.py:151-175

@@ -138,3 +138,16 @@ def test_torch_reference_path_matches_oracle():
     o = O.gated_scan_torch_reference_path(q.float(), k.float(), v.float(), f)
     r = O.gated_scan(*as64(q, k, v, f))
     assert np.abs(o.numpy() - r).max() <= 1e-5 * np.abs(r).max()
+
+
+def test_chunked_ce_golden_is_plain_cross_entropy(golden):
+    """The reference-made chunked CE golden equals torch's cross-entropy over
+    the whole batch (loss and ignored-label handling), on the CPU."""
+    import torch
+    d = golden("chunked_ce")
+    h = torch.from_numpy(d["hidden"]).double()
+    w = torch.from_numpy(d["weight"]).double()
+    lab = torch.from_numpy(d["labels"]).reshape(-1)
+    logits = h.reshape(-1, h.shape[-1]) @ w.t()
+    ref = torch.nn.functional.cross_entropy(logits, lab, reduction="sum") / lab.numel()
+    assert abs(float(ref) - float(d["loss"])) <= 1e-5 * abs(float(ref))
