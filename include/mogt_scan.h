@@ -237,6 +237,26 @@ int mogt_diag_scan_norm_fwd(const void* V, const float* z, int64_t z_per_token, 
                             int in_dtype, int out_dtype, void* status, void* scratch,
                             size_t scratch_bytes, void* stream);
 
+/* Backward of mogt_diag_scan_norm_fwd: gradients of L = sum <y, dy> with
+ * respect to V, z, norm_weight and H0 (the chain rule the reference's
+ * autograd takes through model_mogt.py:168-240 and affine_scan.py:65-124).
+ *   V, z, z_per_token, damping, norm_weight, eps: the forward's arguments;
+ *   dy : [B, L, R*C] in dy_dtype (bf16 or f32);
+ *   fwd_scratch : the forward's `scratch` after that call (it holds the
+ *             state entering each of the forward's chunks), unchanged since;
+ *   dV : [B, L, R, C] in V's dtype; dz : [B, L, z_per_token] f32;
+ *   d_norm_weight : [R*C] f32; dH0 : [B, R, C] f32 or NULL;
+ *   scratch : >= mogt_diag_scan_norm_bwd_scratch_bytes(B, L, R, C) bytes.
+ *   R*C <= 1024.  Reverse-time chunked (8-token chunks): chunk-local adjoint
+ *   aggregates, the adjoint carry per channel, then the gradients. */
+size_t mogt_diag_scan_norm_bwd_scratch_bytes(int64_t B, int64_t L, int64_t R, int64_t C);
+int mogt_diag_scan_norm_bwd(const void* V, const float* z, int64_t z_per_token, float damping,
+                            const float* norm_weight, float eps, const void* dy,
+                            const void* fwd_scratch, void* dV, float* dz, float* d_norm_weight,
+                            float* dH0, int64_t B, int64_t L, int64_t R, int64_t C, int in_dtype,
+                            int dy_dtype, void* status, void* scratch, size_t scratch_bytes,
+                            void* stream);
+
 /* ---------------------------------------------------------------------------
  * Connection map of the MOGT block (replaces model_mogt.py:79-102,
  * _build_transport: torch.matrix_exp / torch.linalg.solve on [B, L, r, r]).

@@ -43,6 +43,9 @@ SIGNATURES = {
     "mogt_diag_scan_norm_scratch_bytes": (_sz, [_i64] * 4 + [_int]),
     "mogt_diag_scan_norm_fwd": (_int, [_vp, _vp, _i64, ctypes.c_float, _vp, _vp, ctypes.c_float, _vp, _vp]
                                 + [_i64] * 4 + [_int, _int, _vp, _vp, _sz, _vp]),
+    "mogt_diag_scan_norm_bwd_scratch_bytes": (_sz, [_i64] * 4),
+    "mogt_diag_scan_norm_bwd": (_int, [_vp, _vp, _i64, ctypes.c_float, _vp, ctypes.c_float, _vp, _vp, _vp, _vp,
+                                       _vp, _vp] + [_i64] * 4 + [_int, _int, _vp, _vp, _sz, _vp]),
     "mogt_connection_map": (_int, [_vp, _vp, _i64, _i64, _int, _int, ctypes.c_float, ctypes.c_float, _int, _int, _vp]),
     "mogt_ce_rows_fwd": (_int, [_vp, _vp, _i64, _i64, _vp, _vp, _vp]),
     "mogt_ce_rows_bwd": (_int, [_vp, _vp, _vp, _i64, _i64, ctypes.c_float, _vp]),

@@ -122,15 +122,16 @@ class MOGTBlock(nn.Module):
         """The identity connection with the forget gate coupled to the value
         gate makes U_t diagonal: the scan and norm_out then run as one fused
         kernel (mogt_diag_scan_norm_fwd) without materialising U or the fp32
-        states.  Forward-only: used when no gradient is recorded and the
-        default B200 scan is in use."""
+        states; with autograd on, its reverse-time chunked backward
+        (mogt_diag_scan_norm_bwd) gives the gradients.  Used with the default
+        B200 scan."""
         return (getattr(self, "fused_identity_scan", True)
                 and getattr(self, "connection_impl", "matrix_exp") == "identity"
                 and gate_lin is not None
                 and getattr(self, "couple_forget_to_value_gate", False)
                 and self.scan_fn is _b200_scan
                 and x.is_cuda
-                and not torch.is_grad_enabled())
+                and self.c % 2 == 0 and (self.r * self.c) % 64 == 0 and self.r * self.c <= 1024)
 
     def _gate_logits(self, x_norm, prefix, gate_lin):
         """phi_value_gate(value_gate_input(x_norm, prefix)) without building
@@ -175,7 +176,11 @@ class MOGTBlock(nn.Module):
         if self._fused_identity_path(x, gate_lin):
             with torch.autograd.profiler.record_function("mogt.value_projection"):
                 V = self.phi_val(x_norm).view(B, L, self.r, self.c)
-                z = self._gate_logits(x_norm, prefix_condition, gate_lin)
+                if torch.is_grad_enabled():
+                    # the concatenated-input linear, differentiable as is
+                    z = gate_lin(self.value_gate_input(x_norm, prefix_condition)).float()
+                else:
+                    z = self._gate_logits(x_norm, prefix_condition, gate_lin)
                 if z.size(-1) not in (1, self.r):
                     raise ValueError("phi_value_gate must output 1 or r gates")
                 z = torch.sigmoid(z)
@@ -183,9 +188,13 @@ class MOGTBlock(nn.Module):
                 # the readout GEMM consumes bf16 under bf16 autocast: write that directly
                 y_dtype = (torch.bfloat16 if torch.is_autocast_enabled("cuda")
                            and torch.get_autocast_dtype("cuda") == torch.bfloat16 else torch.float32)
-                y, _ = ops.diag_scan_norm(V, z, self.norm_out.weight,
-                                          damping=float(getattr(self, "connection_damping", 0.999)),
-                                          eps=self.norm_out.eps, output_dtype=y_dtype)
+                damping = float(getattr(self, "connection_damping", 0.999))
+                if torch.is_grad_enabled():
+                    y = ops.DiagScanNormFn.apply(V, z, self.norm_out.weight, None, damping,
+                                                 self.norm_out.eps, y_dtype)
+                else:
+                    y, _ = ops.diag_scan_norm(V, z, self.norm_out.weight, damping=damping,
+                                              eps=self.norm_out.eps, output_dtype=y_dtype)
             with torch.autograd.profiler.record_function("mogt.readout"):
                 x = x + self.theta_read(y.view(B, L, D))
             with torch.autograd.profiler.record_function("mogt.ffn"):

@@ -314,6 +314,10 @@ int run(const void* V, const float* z, const float* H0, const float* w, float ep
 
 inline int elt_size(int dt) { return dt == MOGT_DTYPE_F32 ? 4 : 2; }
 
+// the forward's chunk length, for the backward (diag_bwd.cu), which reads the
+// forward's per-chunk carries
+int forward_chunk_len(int64_t D, int in_dtype) { return chunk_len(D, elt_size(in_dtype)); }
+
 }  // namespace diag
 }  // namespace mogt
 

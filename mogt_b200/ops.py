@@ -15,6 +15,7 @@ import torch
 from . import _native as N
 
 __all__ = ["gated_scan_fwd", "gated_scan_bwd", "matrix_scan_fwd", "matrix_scan_bwd", "diag_scan_norm",
+           "diag_scan_norm_bwd", "DiagScanNormFn",
            "affine_scan", "affine_grad_u", "gated_num_chunks"]
 
 
@@ -241,7 +242,7 @@ def matrix_scan_bwd(A, q, k, v, f, do, saved, *, want_dS0=False):
 
 
 def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=None,
-                   output_dtype=None, want_final=False):
+                   output_dtype=None, want_final=False, return_scratch=False):
     """Fused identity-connection MOGT scan and RMSNorm readout:
     h_t = damping (1 - z_t[row]) h_{t-1} + V_t z_t[row] per channel (V times z
     rounded in V's dtype, as V * z.to(V.dtype) does), then per token
@@ -280,7 +281,64 @@ def diag_scan_norm(V, z, norm_weight, *, damping=1.0, eps=1e-6, initial_state=No
                                         N.ptr(scratch), scratch.numel(), N.stream_ptr(dev))
         N.check(st, "mogt_diag_scan_norm_fwd")
         wse.after_launch("mogt_diag_scan_norm_fwd")
+    if return_scratch:
+        return y, Hf, scratch
     return y, Hf
+
+
+def diag_scan_norm_bwd(V, z, norm_weight, dy, fwd_scratch, *, damping=1.0, eps=1e-6, want_dH0=False):
+    """Gradients of sum(y * dy) for y = diag_scan_norm(V, z, norm_weight, ...):
+    returns (dV in V's dtype, dz fp32 shaped like z, d_norm_weight fp32,
+    dH0 fp32 [B, R, C] or None).  `fwd_scratch` is the third result of
+    diag_scan_norm(..., return_scratch=True) on the same inputs."""
+    _require_cuda(V, z, norm_weight, dy, fwd_scratch, what="diag_scan_norm backward")
+    B, L, R, C = V.shape
+    zz = z.reshape(B, L, -1).to(torch.float32).contiguous()
+    V = V.contiguous()
+    dy = dy.reshape(B, L, R * C)
+    if dy.dtype not in (torch.bfloat16, torch.float32):
+        dy = dy.float()
+    dy = dy.contiguous()
+    w = norm_weight.to(torch.float32).contiguous()
+    dev = V.device
+    dV = torch.empty_like(V)
+    dz = torch.empty(B, L, zz.shape[-1], dtype=torch.float32, device=dev)
+    dw = torch.empty(R * C, dtype=torch.float32, device=dev)
+    dH0 = torch.empty(B, R, C, dtype=torch.float32, device=dev) if want_dH0 else None
+    L_ = N.lib()
+    nbytes = L_.mogt_diag_scan_norm_bwd_scratch_bytes(B, L, R, C)
+    with torch.cuda.device(dev):
+        scratch = torch.empty(max(nbytes, 16), dtype=torch.uint8, device=dev)
+        wse = N.workspaces.entry(dev, 256, "diag_bwd")
+        st = L_.mogt_diag_scan_norm_bwd(N.ptr(V), N.ptr(zz), zz.shape[-1], float(damping), N.ptr(w), float(eps),
+                                        N.ptr(dy), N.ptr(fwd_scratch), N.ptr(dV), N.ptr(dz), N.ptr(dw), N.ptr(dH0),
+                                        B, L, R, C, N.dtype_code(V.dtype), N.dtype_code(dy.dtype),
+                                        N.ptr(wse.buf), N.ptr(scratch), scratch.numel(), N.stream_ptr(dev))
+        N.check(st, "mogt_diag_scan_norm_bwd")
+        wse.after_launch("mogt_diag_scan_norm_bwd")
+    return dV, dz.view(z.shape), dw.view(norm_weight.shape).to(norm_weight.dtype), dH0
+
+
+class DiagScanNormFn(torch.autograd.Function):
+    """Autograd for diag_scan_norm: the forward keeps its chunk carries for the
+    reverse-time chunked backward (mogt_diag_scan_norm_bwd)."""
+
+    @staticmethod
+    def forward(ctx, V, z, norm_weight, initial_state, damping, eps, output_dtype):
+        y, _, scratch = diag_scan_norm(V, z, norm_weight, damping=damping, eps=eps,
+                                       initial_state=initial_state, output_dtype=output_dtype,
+                                       return_scratch=True)
+        ctx.save_for_backward(V, z, norm_weight, scratch)
+        ctx.damping, ctx.eps = damping, eps
+        ctx.has_h0 = initial_state is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        V, z, w, scratch = ctx.saved_tensors
+        dV, dz, dw, dH0 = diag_scan_norm_bwd(V, z, w, dy, scratch, damping=ctx.damping, eps=ctx.eps,
+                                             want_dH0=ctx.has_h0 and ctx.needs_input_grad[3])
+        return dV, dz.to(z.dtype), dw, dH0, None, None, None
 
 
 def _check_uv(U, V):
