@@ -161,6 +161,34 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase) {
   }
 }
 
+// Bounded parity wait without a suspend hint: each probe returns after a
+// short hardware-chosen interval, so a waiting warp resumes as soon as the
+// phase completes.  Same time limit and return value as mbar_wait.
+__device__ __forceinline__ bool mbar_try_wait_spin(uint32_t addr, uint32_t phase) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(addr), "r"(phase)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t phase) {
+  const uint32_t addr = smem_u32(bar);
+  if (mbar_try_wait_spin(addr, phase)) return true;
+  const uint64_t t0 = global_ns();
+  for (;;) {
+    if (mbar_try_wait_spin(addr, phase)) return true;
+    if (global_ns() - t0 > kWaitLimitNs) return false;
+  }
+}
+
+// 32-bit global store with an L2 eviction-priority hint (a createpolicy value).
+__device__ __forceinline__ void st_global_hint(void* p, uint32_t v, uint64_t pol) {
+  asm volatile("st.global.L2::cache_hint.b32 [%0], %1, %2;" ::"l"(p), "r"(v), "l"(pol) : "memory");
+}
+
 // 3-D tiled TMA load (no multicast) into shared memory, completion counted on
 // `bar` in bytes.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
@@ -203,6 +231,20 @@ __device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(addr));
+}
+
+// Ordered forms (volatile, memory clobber) for tiles that TMA or the tensor
+// core also touch: they stay after the waits and before the fences around them.
+__device__ __forceinline__ void ldsm_x4_v(uint32_t (&r)[4], uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void stsm_x4(uint32_t addr, const uint32_t (&r)[4]) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1,%2,%3,%4};" ::"r"(addr),
+               "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3])
+               : "memory");
 }
 
 __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], uint32_t addr) {

@@ -539,7 +539,7 @@ size_t mogt_gated_scan_fwd_workspace_bytes(int64_t BH, int64_t T, int64_t dk, in
                                            int in_dtype) {
   if (in_dtype != MOGT_DTYPE_BF16 || dk != D || dv != D || T <= 0 || BH <= 0)
     return sizeof(WsHeader);
-  return ws_layout((size_t)BH * make_plan(BH, T, 2 * sm_count()).nstripes).total;
+  return chunked_fwd_workspace_bytes(BH, T);
 }
 
 // Checks every argument of a bf16 forward call and, when it is valid, returns
@@ -576,23 +576,15 @@ static int prepare_kernels() {
   return MOGT_OK;
 }
 
-int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
-                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
-                        int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
-                        void* workspace, size_t workspace_bytes, void* stream) {
-  if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
-  if (T == 0) return MOGT_OK;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (in_dtype == MOGT_DTYPE_F32) {
-    if (!k || !v || !f || (o && !q)) return MOGT_ERR_ARG;
-    if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
-    if (out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
-    if (chunk_states) return MOGT_ERR_UNSUPPORTED;
-    return launch_fwd_seq(static_cast<const float*>(q), static_cast<const float*>(k),
-                          static_cast<const float*>(v), f, static_cast<float*>(o), S0, S_final,
-                          decay_final, (int)BH, (int)T, (int)dk, (int)dv, s);
-  }
-  if (in_dtype != MOGT_DTYPE_BF16) return MOGT_ERR_DTYPE;
+}  // extern "C"
+
+// The stripe kernel (one CTA per stripe, decoupled look-back between the
+// stripes of a head): its workspace is the small look-back layout, so the
+// allocation-free entry point runs it on its fixed scratch.
+static int stripe_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
+                      const float* S0, float* S_final, float* decay_final, void* chunk_states,
+                      int64_t BH, int64_t T, int64_t dk, int64_t dv, int out_dtype,
+                      void* workspace, size_t workspace_bytes, cudaStream_t s) {
   Plan pl;
   WsLayout L;
   const int vs = validate_bf16_fwd(q, k, v, f, o, BH, T, dk, dv, out_dtype, &pl, &L);
@@ -637,6 +629,33 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   else
     gated_fwd_stripe<false><<<(unsigned)NU, NTHREADS, SM_ALLOC, s>>>(maps[0], maps[1], maps[2], P);
   return mogt_host::launch_status();
+}
+
+extern "C" {
+
+int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
+                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
+                        int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
+                        void* workspace, size_t workspace_bytes, void* stream) {
+  if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
+  if (T == 0) return MOGT_OK;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (in_dtype == MOGT_DTYPE_F32) {
+    if (!k || !v || !f || (o && !q)) return MOGT_ERR_ARG;
+    if (BH >= ((int64_t)1 << 31) || T >= ((int64_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
+    if (out_dtype != MOGT_DTYPE_F32) return MOGT_ERR_DTYPE;
+    if (chunk_states) return MOGT_ERR_UNSUPPORTED;
+    return launch_fwd_seq(static_cast<const float*>(q), static_cast<const float*>(k),
+                          static_cast<const float*>(v), f, static_cast<float*>(o), S0, S_final,
+                          decay_final, (int)BH, (int)T, (int)dk, (int)dv, s);
+  }
+  if (in_dtype != MOGT_DTYPE_BF16) return MOGT_ERR_DTYPE;
+  Plan pl;
+  WsLayout L;
+  const int vs = validate_bf16_fwd(q, k, v, f, o, BH, T, dk, dv, out_dtype, &pl, &L);
+  if (vs != MOGT_OK) return vs;
+  return launch_chunked_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T,
+                            out_dtype, workspace, workspace_bytes, s);
 }
 
 }  // extern "C"
@@ -701,8 +720,8 @@ extern "C" int mogt_gated_scan_fwd_noalloc(const void* q, const void* k, const v
     if (!scratch) return MOGT_ERR_LAUNCH;
     if (cudaMemsetAsync(scratch + L.flags, 0, L.a_agg - L.flags, s) != cudaSuccess)
       return MOGT_ERR_LAUNCH;
-    return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk,
-                               dv, in_dtype, out_dtype, scratch, kStaticScratchBytes, stream);
+    return stripe_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk, dv,
+                      out_dtype, scratch, kStaticScratchBytes, s);
   }
   // the fp32 path uses no scratch
   return mogt_gated_scan_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T, dk, dv,

@@ -11,6 +11,14 @@ int launch_fwd_seq(const float* q, const float* k, const float* v, const float* 
                    const float* S0, float* S_final, float* decay_final, int BH, int T, int dk,
                    int dv, cudaStream_t s);
 
+// Chunk-parallel bf16 forward (gated_fwd_chunked.cu): segment-local chunk
+// states, segment carries, then every chunk's outputs independently.
+size_t chunked_fwd_workspace_bytes(int64_t BH, int64_t T);
+int launch_chunked_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
+                       const float* S0, float* S_final, float* decay_final, void* chunk_states,
+                       int64_t BH, int64_t T, int out_dtype, void* workspace,
+                       size_t workspace_bytes, cudaStream_t s);
+
 
 }  // namespace gated
 }  // namespace mogt
