@@ -38,6 +38,11 @@ namespace mogt {
 namespace gated {
 namespace chunked {
 
+// Programmatic dependent launch: a dependent kernel may start early and waits
+// here for the complete results of the kernel before it.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // Fragment tiles moved with ldmatrix / stmatrix.  A thread's accumulator
 // fragment (tcgen05.ld 16x256b, warp w = rows 16w..16w+15) is, per 32-column
 // half h, the m16n8 layout of four 8x8 blocks per row half; x4 number x of
@@ -114,6 +119,7 @@ __global__ void __launch_bounds__(NTHREADS, A_CTAS_PER_SM)
   uint64_t* dsb = full + A_RS;
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + A_SM_TSLOT);
 
+  griddep_launch();
   if (warp == 0) tmem_alloc(tslot, A_NB * 64);
   if (tid == 0) {
 #pragma unroll
@@ -241,40 +247,78 @@ __global__ void __launch_bounds__(NTHREADS, A_CTAS_PER_SM)
 }
 
 // ---------------------------------------------------------------------------
-// gated_seg_carry: one thread per state element, sequential over segments
+// gated_seg_carry: the state entering every segment.  A CTA owns 32 state
+// elements of one head (lane = element, coalesced) and its 8 warps split the
+// segments into 8 consecutive groups: each group's affine composite (decay,
+// sum) is formed in parallel, the groups are chained through shared memory,
+// then every group re-runs its segments from its incoming state (the second
+// reads hit L2).
 // ---------------------------------------------------------------------------
-__global__ void __launch_bounds__(256) gated_seg_carry(const float* __restrict__ seg_agg,
-                                                       const float* __restrict__ seg_lam,
-                                                       float* __restrict__ seg_state,
-                                                       const float* __restrict__ S0,
-                                                       float* __restrict__ S_final,
-                                                       float* __restrict__ decay_final, int nseg) {
-  const int bh = blockIdx.y;
-  const int e = blockIdx.x * blockDim.x + threadIdx.x;
-  float s = S0 ? S0[(size_t)bh * (D * D) + e] : 0.f;
-  float lsum = 0.f;
+constexpr int C_WARPS = 8;
+
+__global__ void __launch_bounds__(32 * C_WARPS) gated_seg_carry(const float* __restrict__ seg_agg,
+                                                             const float* __restrict__ seg_lam,
+                                                             float* __restrict__ seg_state,
+                                                             const float* __restrict__ S0,
+                                                             float* __restrict__ S_final,
+                                                             float* __restrict__ decay_final,
+                                                             int nseg) {
+  __shared__ float grp_l[C_WARPS];
+  __shared__ float grp_b[C_WARPS][32];
+  griddep_launch();
+  griddep_wait();   // the segment aggregates of gated_chunk_local
+  const int bh = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = blockIdx.x * 32 + lane;
+  const int G = (nseg + C_WARPS - 1) / C_WARPS;
+  const int g0 = min(nseg, warp * G), g1 = min(nseg, g0 + G);
   const size_t b0 = (size_t)bh * nseg;
-  // aggregates in batches of 8 independent loads ahead of the dependent chain
-  constexpr int NBATCH = 8;
-  for (int g0 = 0; g0 < nseg; g0 += NBATCH) {
-    float ag[NBATCH], lg[NBATCH];
+  // pass 1: this group's composite
+  float lsum = 0.f, bsum = 0.f;
+  for (int g = g0; g < g1; g += 8) {
+    float ag[8], lg[8];
 #pragma unroll
-    for (int q = 0; q < NBATCH; ++q) {
-      const bool in = g0 + q < nseg;
-      ag[q] = in ? __ldg(seg_agg + (b0 + g0 + q) * (D * D) + e) : 0.f;
-      lg[q] = in ? __ldg(seg_lam + b0 + g0 + q) : 0.f;
+    for (int q = 0; q < 8; ++q) {
+      const bool in = g + q < g1;
+      ag[q] = in ? __ldg(seg_agg + (b0 + g + q) * (D * D) + e) : 0.f;
+      lg[q] = in ? __ldg(seg_lam + b0 + g + q) : 0.f;
     }
 #pragma unroll
-    for (int q = 0; q < NBATCH; ++q) {
-      if (g0 + q < nseg) {
-        seg_state[(b0 + g0 + q) * (D * D) + e] = s;
-        lsum += lg[q];
-        s = fmaf(fast_exp2(lg[q]), s, ag[q]);
-      }
+    for (int q = 0; q < 8; ++q) {
+      lsum += lg[q];
+      bsum = fmaf(fast_exp2(lg[q]), bsum, ag[q]);
     }
   }
-  if (S_final) S_final[(size_t)bh * (D * D) + e] = s;
-  if (decay_final && e == 0) decay_final[bh] = fast_exp2(lsum);
+  grp_l[warp] = lsum;   // identical in every lane
+  grp_b[warp][lane] = bsum;
+  __syncthreads();
+  // state entering this group
+  float s = S0 ? S0[(size_t)bh * (D * D) + e] : 0.f;
+  float ltot = 0.f;
+  for (int w = 0; w < warp; ++w) {
+    s = fmaf(fast_exp2(grp_l[w]), s, grp_b[w][lane]);
+    ltot += grp_l[w];
+  }
+  // pass 2: the state entering every segment of the group
+  for (int g = g0; g < g1; g += 8) {
+    float ag[8], lg[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const bool in = g + q < g1;
+      ag[q] = in ? __ldg(seg_agg + (b0 + g + q) * (D * D) + e) : 0.f;
+      lg[q] = in ? __ldg(seg_lam + b0 + g + q) : 0.f;
+    }
+#pragma unroll
+    for (int q = 0; q < 8; ++q)
+      if (g + q < g1) {
+        seg_state[(b0 + g + q) * (D * D) + e] = s;
+        s = fmaf(fast_exp2(lg[q]), s, ag[q]);
+      }
+  }
+  if (warp == C_WARPS - 1) {
+    // the last group ends the sequence (empty trailing groups pass s through)
+    if (S_final) S_final[(size_t)bh * (D * D) + e] = s;
+    if (decay_final && e == 0) decay_final[bh] = fast_exp2(ltot + lsum);
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -359,22 +403,27 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
   const bool want_out = p.o != nullptr;
   bool ok = true;
 
+  // roles of single threads: lane 0 of warp 0 issues the output products,
+  // of warp 1 the P products, of warp 3 the TMA loads
+  const bool tma_thr = tid == 96, p_thr = tid == 32, o_thr = tid == 0;
   uint64_t pol_last = 0;
-  if (tid == 0) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_last));
+  if (tma_thr) asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_last));
   // items are taken from the end of the range backwards: the chunks the
   // local pass touched last are the most likely to still be in L2
   auto unit_of = [&](int i) { return u_end - 1 - i; };
-  auto issue = [&](int i) {   // every tile is read for the last time here
+  // every tile is read for the last time here; `part` 1: q, k, v only,
+  // 2: the local state only (issued after the wait on the earlier kernels)
+  auto issue = [&](int i, int part = 0) {
     if (i >= n) return;
     const int u = unit_of(i), bh = u / nchunks, c = u % nchunks;
     uint8_t* base = smem + (i & 1) * B_SLOT;
-    mbar_arrive_expect_tx(&full[i & 1], (want_out ? 4 : 1) * TILE);
-    if (want_out) {
+    if (part != 2) mbar_arrive_expect_tx(&full[i & 1], (want_out ? 4 : 1) * TILE);
+    if (want_out && part != 2) {
       tma_load_3d_hint(base, &tq, &full[i & 1], 0, c * CH, bh, pol_last);
       tma_load_3d_hint(base + TILE, &tk, &full[i & 1], 0, c * CH, bh, pol_last);
       tma_load_3d_hint(base + 2 * TILE, &tv, &full[i & 1], 0, c * CH, bh, pol_last);
     }
-    tma_load_3d_hint(base + 3 * TILE, &tl, &full[i & 1], 0, c * CH, bh, pol_last);
+    if (part != 1) tma_load_3d_hint(base + 3 * TILE, &tl, &full[i & 1], 0, c * CH, bh, pol_last);
   };
   auto issue_p = [&](int i) {   // P_i = Q K^T (raw tiles), one thread
     const uint8_t* base = smem + (i & 1) * B_SLOT;
@@ -382,14 +431,21 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
     umma_commit(bar_p);
   };
 
-  if (tid == 0 && n > 0) {
-    issue(0);
-    issue(1);
-    if (want_out) {
-      if (!mbar_wait_spin(&full[0], 0)) ok = false;
-      tc_fence_after();
-      issue_p(0);
-    }
+  // q, k, v of the first two items do not depend on the earlier kernels of
+  // the forward: their loads overlap the segment-carry kernel
+  if (tma_thr && n > 0) {
+    issue(0, 1);
+    issue(1, 1);
+  }
+  griddep_wait();   // local states, gate tables and segment states are complete
+  if (tma_thr && n > 0) {
+    issue(0, 2);
+    issue(1, 2);
+  }
+  if (p_thr && n > 0 && want_out) {
+    if (!mbar_wait_spin(&full[0], 0)) ok = false;
+    tc_fence_after();
+    issue_p(0);
   }
   __syncwarp();
 
@@ -403,9 +459,16 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
     lam_cur = __ldg(p.lam + u);
   }
   const int t0 = 16 * warp + g, t1 = t0 + 8;   // this thread's rows of a chunk
+  // (head, chunk, segment) of the current item, stepped backwards without divisions
+  int bh = 0, c = 0, seg = 0;
+  if (n > 0) {
+    bh = (u_end - 1) / nchunks;
+    c = (u_end - 1) % nchunks;
+    seg = c / p.cps;
+  }
 
   for (int i = 0; i < n; ++i) {
-    const int u = unit_of(i), bh = u / nchunks, c = u % nchunks;
+    const int u = unit_of(i);
     const int s = i & 1;
     uint8_t* base = smem + s * B_SLOT;
     WGates gt;
@@ -422,7 +485,7 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
     }
     const bool fast = factorises(gt);
     // state of the chunk's segment (changes every cps chunks)
-    const int key = bh * p.nseg + c / p.cps;
+    const int key = bh * p.nseg + seg;
     if (key != cur_key) {
       const float* src = p.seg_state + (size_t)key * (D * D);
       load_frag_rowmajor(sseg[0], src, fa);
@@ -542,13 +605,13 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
     tc_fence_before();
     __syncthreads();
     if (want_out && lane == 0) {
-      if (warp == 0) {
+      if (o_thr) {
         tc_fence_after();
         // O = Q S_in + P'' V
         umma_64x64x64(tbase + TM_O, smem_u32(base), false, smem_u32(base + 3 * TILE), true, false);
         umma_64x64x64(tbase + TM_O, smem_u32(base + TILE), false, smem_u32(base + 2 * TILE), true, true);
         umma_commit(bar_o);
-      } else if (warp == 1 && i + 1 < n) {
+      } else if (p_thr && i + 1 < n) {
         if (!mbar_wait_spin(&full[s ^ 1], ((i + 1) >> 1) & 1)) ok = false;
         tc_fence_after();
         issue_p(i + 1);
@@ -611,8 +674,15 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
       }
     }
     // every read of slot s (threads and products) is done: refill it
-    if (tid == 0) issue(i + 2);
+    if (tma_thr) issue(i + 2);
     __syncwarp();
+    if (--c < 0) {
+      c = nchunks - 1;
+      --bh;
+      seg = c / p.cps;
+    } else if (c < seg * p.cps) {
+      --seg;
+    }
   }
   if (lane == 0) bulk_wait<0>();
 
@@ -735,8 +805,22 @@ int launch_chunked_fwd(const void* q, const void* k, const void* v, const float*
   A.nseg = pl.nstripes;
   gated_chunk_local<<<(unsigned)(BH * pl.nstripes), NTHREADS, A_SM_ALLOC, s>>>(maps[1], maps[2], maps[3], A);
   float* seg_state = reinterpret_cast<float*>(ws + L.seg_state);
-  gated_seg_carry<<<dim3(D * D / 256, (unsigned)BH), 256, 0, s>>>(
-      A.seg_agg, A.seg_lam, seg_state, S0, S_final, decay_final, pl.nstripes);
+  // the carry and output kernels are launched as programmatic dependents: they
+  // may start while the previous kernel drains and wait for its results with
+  // griddepcontrol.wait
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(D * D / 32, (unsigned)BH);
+  cfg.blockDim = dim3(32 * C_WARPS);
+  cfg.dynamicSmemBytes = 0;
+  cfg.stream = s;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, gated_seg_carry, (const float*)A.seg_agg, (const float*)A.seg_lam,
+                         seg_state, S0, S_final, decay_final, pl.nstripes) != cudaSuccess)
+    return MOGT_ERR_LAUNCH;
   if (!need_out) return mogt_host::launch_status();
 
   BParams Bp;
@@ -755,10 +839,14 @@ int launch_chunked_fwd(const void* q, const void* k, const void* v, const float*
   const int max_ctas = B_CTAS_PER_SM * sm_count();
   Bp.per_cta = (Bp.nunits + max_ctas - 1) / max_ctas;
   const unsigned grid = (unsigned)((Bp.nunits + Bp.per_cta - 1) / Bp.per_cta);
-  if (out_dtype == MOGT_DTYPE_F32)
-    gated_chunk_out<true><<<grid, B_THREADS, B_SM_ALLOC, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], Bp);
-  else
-    gated_chunk_out<false><<<grid, B_THREADS, B_SM_ALLOC, s>>>(maps[0], maps[1], maps[2], maps[3], maps[4], Bp);
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(B_THREADS);
+  cfg.dynamicSmemBytes = B_SM_ALLOC;
+  const cudaError_t e =
+      out_dtype == MOGT_DTYPE_F32
+          ? cudaLaunchKernelEx(&cfg, gated_chunk_out<true>, maps[0], maps[1], maps[2], maps[3], maps[4], Bp)
+          : cudaLaunchKernelEx(&cfg, gated_chunk_out<false>, maps[0], maps[1], maps[2], maps[3], maps[4], Bp);
+  if (e != cudaSuccess) return MOGT_ERR_LAUNCH;
   return mogt_host::launch_status();
 }
 
