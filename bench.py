@@ -224,12 +224,17 @@ class ClockSampler:
                 "reasons": reasons, "samples": len(inside)}
 
 
-# DRAM bytes (read + write) of one launch of the forward kernel at the bench
-# workload, from one ncu capture of that launch (dram__bytes_read.sum +
-# dram__bytes_write.sum; the command is in the forward kernel's profile
-# summary).  Updated by hand when the kernel changes; None when no capture
-# of the current kernel exists.
-FWD_TRAFFIC_BYTES_PER_LAUNCH = 258156800
+# One forward at the bench workload is three launches: gated_chunk_local,
+# gated_seg_carry and gated_chunk_out (chained by programmatic dependent
+# launch).  The roofline treats the three as the unit: achieved = algorithmic
+# bytes / event time of the whole forward.  Traffic is their summed DRAM bytes
+# (dram__bytes_read.sum + dram__bytes_write.sum) from one ncu capture of each
+# kernel without cache flushing, so that the output pass's L2 hits on what the
+# local pass left behind count as they do in the timed loop; the command is in
+# the forward's profile summary.  Updated by hand when the kernels change;
+# None when no capture of the current kernels exists.
+FWD_KERNELS = ("gated_chunk_local", "gated_seg_carry", "gated_chunk_out")
+FWD_TRAFFIC_BYTES_PER_LAUNCH = 367570688
 
 
 def measured_peak_hbm():
@@ -409,13 +414,14 @@ def run_b200(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": traffic,
                      "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
-                     "algorithmic_bytes_per_launch": alg_bytes},
+                     "algorithmic_bytes_per_launch": alg_bytes,
+                     "kernels": "+".join(FWD_KERNELS) + " (one forward)"},
         "cpu_baseline": cpu,
         "e2e": {"value": e2e_value, "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": e2e_steps, "ms_per_step": e2e_ms / e2e_steps,
                 "api": "mogt_b200.gated_scan", "matches_device_result": bool(ok),
                 "pipelining": "copy-out of step i on a second stream overlaps step i+1's copy-in and scan"},
-        "gpu_launches": args.steps,
+        "gpu_launches": args.steps * len(FWD_KERNELS),
         "clocks": clocks.summary(t_wall0, t_wall1),
         "workspace_errors": errs,
     }
@@ -608,19 +614,35 @@ def extra_connection(dev):
 def extra_config2_sweep(dev):
     """BASELINE config 2 at T = 8192 and 16384 (the bench line is T = 32768):
     forward and backward timed separately, 516 / 904 algorithmic bytes per
-    (token, head)."""
-    from mogt_b200 import ops
+    (token, head).  The forward is timed through the C ABI with preallocated
+    buffers, as the bench line is (the Python wrapper's per-call host work
+    would otherwise set the pace at these sizes); the backward through
+    mogt_b200.ops (its output allocation included)."""
+    from mogt_b200 import _native, ops
     import torch
+    L = _native.lib()
     out = {}
     for T in (8192, 16384):
         q, k, v, f = (t.to(dev) for t in make_inputs(1, 12, T, 7000 + T))
+        o = torch.empty(1, 12, T, 64, dtype=torch.bfloat16, device=dev)
+        nbytes = L.mogt_gated_scan_fwd_workspace_bytes(12, T, 64, 64, _native.BF16)
+        ws = torch.zeros(nbytes, dtype=torch.uint8, device=dev)
+        stream = _native.ctypes.c_void_p(torch.cuda.current_stream(dev).cuda_stream)
+
+        def fwd():
+            st = L.mogt_gated_scan_fwd(_native.ptr(q), _native.ptr(k), _native.ptr(v), _native.ptr(f),
+                                       _native.ptr(o), None, None, None, None, 12, T, 64, 64,
+                                       _native.BF16, _native.BF16, _native.ptr(ws), nbytes, stream)
+            if st != 0:
+                raise RuntimeError(f"mogt_gated_scan_fwd failed: {st}")
+        ms_f = _time_call(fwd, 50, warm=5)
         g = torch.randn(1, 12, T, 64, generator=torch.Generator().manual_seed(T)).to(dev).bfloat16()
-        ms_f = _time_call(lambda: ops.gated_scan_fwd(q, k, v, f), 20)
         _, _, _, cs = ops.gated_scan_fwd(q, k, v, f, save_states=True)
         ms_b = _time_call(lambda: ops.gated_scan_bwd(q, k, v, f, g, chunk_states=cs), 20)
         out[f"T{T}"] = {"fwd_ms": ms_f, "fwd_tokens_per_s": T / (ms_f / 1e3),
                         "fwd_GBps": 516 * 12 * T / (ms_f / 1e3) / 1e9,
                         "bwd_ms": ms_b, "bwd_GBps": 904 * 12 * T / (ms_b / 1e3) / 1e9}
+        del ws, o
     return out
 
 

@@ -86,6 +86,23 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
                         int64_t BH, int64_t T, int64_t dk, int64_t dv, int in_dtype, int out_dtype,
                         void* workspace, size_t workspace_bytes, void* stream);
 
+/* Second half of a bf16 forward whose first half already ran: the segment
+ * carry from the initial state S0 and the output pass, reusing the chunk-local
+ * states that an earlier mogt_gated_scan_fwd call with the same k, v, f, BH,
+ * T and workspace left there (that call may be state-only, o = NULL, and must
+ * have been made with chunk_states = NULL; nothing may use the workspace in
+ * between).  The sequence-parallel scan uses it: each rank's state-only pass
+ * gives its segment carry, and after the carries are exchanged the output
+ * pass resumes from the incoming state without re-reading k, v for the local
+ * states.  Arguments as mogt_gated_scan_fwd; in_dtype must be MOGT_DTYPE_BF16.
+ * Replaces the second full forward of the segment (the reference has no
+ * sequence-parallel path; its carry algebra is affine_scan.py:250-271). */
+int mogt_gated_scan_fwd_resume(const void* q, const void* k, const void* v, const float* f,
+                               void* o, const float* S0, float* S_final, float* decay_final,
+                               void* chunk_states, int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                               int in_dtype, int out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Allocation-free variant of mogt_gated_scan_fwd.  This entry point has no
  * counterpart in the reference.  It exists for callers that cannot allocate
  * device memory: hosts whose device memory is owned by an allocator or a

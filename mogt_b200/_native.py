@@ -31,6 +31,7 @@ SIGNATURES = {
     "mogt_gated_scan_num_chunks": (_i64, [_i64, _i64, _i64, _int]),
     "mogt_gated_scan_fwd_workspace_bytes": (_sz, [_i64, _i64, _i64, _i64, _int]),
     "mogt_gated_scan_fwd": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp, _sz, _vp]),
+    "mogt_gated_scan_fwd_resume": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp, _sz, _vp]),
     "mogt_gated_scan_fwd_noalloc": (_int, [_vp] * 9 + [_i64] * 4 + [_int, _int, _vp]),
     "mogt_gated_scan_fwd_noalloc_status": (_int, [_vp, ctypes.POINTER(_int), ctypes.POINTER(ctypes.c_uint32)]),
     "mogt_gated_scan_bwd_workspace_bytes": (_sz, [_i64] * 4 + [_int]),

@@ -655,7 +655,24 @@ int mogt_gated_scan_fwd(const void* q, const void* k, const void* v, const float
   const int vs = validate_bf16_fwd(q, k, v, f, o, BH, T, dk, dv, out_dtype, &pl, &L);
   if (vs != MOGT_OK) return vs;
   return launch_chunked_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T,
-                            out_dtype, workspace, workspace_bytes, s);
+                            out_dtype, workspace, workspace_bytes, s, false);
+}
+
+int mogt_gated_scan_fwd_resume(const void* q, const void* k, const void* v, const float* f,
+                               void* o, const float* S0, float* S_final, float* decay_final,
+                               void* chunk_states, int64_t BH, int64_t T, int64_t dk, int64_t dv,
+                               int in_dtype, int out_dtype, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (BH <= 0 || T < 0 || dk <= 0 || dv <= 0) return MOGT_ERR_SHAPE;
+  if (T == 0) return MOGT_OK;
+  if (in_dtype != MOGT_DTYPE_BF16) return MOGT_ERR_UNSUPPORTED;
+  Plan pl;
+  WsLayout L;
+  const int vs = validate_bf16_fwd(q, k, v, f, o, BH, T, dk, dv, out_dtype, &pl, &L);
+  if (vs != MOGT_OK) return vs;
+  return launch_chunked_fwd(q, k, v, f, o, S0, S_final, decay_final, chunk_states, BH, T,
+                            out_dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream),
+                            true);
 }
 
 }  // extern "C"

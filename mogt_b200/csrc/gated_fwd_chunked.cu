@@ -743,7 +743,7 @@ size_t chunked_fwd_workspace_bytes(int64_t BH, int64_t T) {
 int launch_chunked_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
                        int64_t BH, int64_t T, int out_dtype, void* workspace,
-                       size_t workspace_bytes, cudaStream_t s) {
+                       size_t workspace_bytes, cudaStream_t s, bool resume) {
   using namespace chunked;
   const Plan pl = make_plan(BH, T, A_CTAS_PER_SM * sm_count());
   const Layout L = layout((size_t)BH, pl);
@@ -767,9 +767,11 @@ int launch_chunked_fwd(const void* q, const void* k, const void* v, const float*
       return MOGT_ERR_LAUNCH;
   }
   // segment-local states: into chunk_states when the caller keeps them (the
-  // output pass overwrites each with the full entering state), else workspace
-  __nv_bfloat16* Lst = chunk_states ? static_cast<__nv_bfloat16*>(chunk_states)
-                                    : reinterpret_cast<__nv_bfloat16*>(ws + L.Lst);
+  // output pass overwrites each with the full entering state), else workspace.
+  // A resumed call finds them in the workspace, where the earlier call
+  // (made without chunk_states) left them.
+  __nv_bfloat16* Lst = (chunk_states && !resume) ? static_cast<__nv_bfloat16*>(chunk_states)
+                                                 : reinterpret_cast<__nv_bfloat16*>(ws + L.Lst);
   {
     cuuint64_t dims[3] = {(cuuint64_t)D, (cuuint64_t)pl.nchunks * CH, (cuuint64_t)BH};
     cuuint64_t strides[2] = {(cuuint64_t)D * 2, (cuuint64_t)pl.nchunks * CH * D * 2};
@@ -803,7 +805,8 @@ int launch_chunked_fwd(const void* q, const void* k, const void* v, const float*
   A.nchunks = pl.nchunks;
   A.cps = pl.cps;
   A.nseg = pl.nstripes;
-  gated_chunk_local<<<(unsigned)(BH * pl.nstripes), NTHREADS, A_SM_ALLOC, s>>>(maps[1], maps[2], maps[3], A);
+  if (!resume)
+    gated_chunk_local<<<(unsigned)(BH * pl.nstripes), NTHREADS, A_SM_ALLOC, s>>>(maps[1], maps[2], maps[3], A);
   float* seg_state = reinterpret_cast<float*>(ws + L.seg_state);
   // the carry and output kernels are launched as programmatic dependents: they
   // may start while the previous kernel drains and wait for its results with

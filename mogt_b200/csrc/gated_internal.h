@@ -17,7 +17,7 @@ size_t chunked_fwd_workspace_bytes(int64_t BH, int64_t T);
 int launch_chunked_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
                        int64_t BH, int64_t T, int out_dtype, void* workspace,
-                       size_t workspace_bytes, cudaStream_t s);
+                       size_t workspace_bytes, cudaStream_t s, bool resume);
 
 
 }  // namespace gated

@@ -30,7 +30,7 @@ def gated_num_chunks(T: int, dk: int, dv: int, dtype: torch.dtype) -> int:
 
 
 def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_final=False,
-                   save_states=False, want_output=True):
+                   save_states=False, want_output=True, resume=False):
     """o_t = S_t^T q_t with S_t = f_t S_{t-1} + (1-f_t) k_t v_t^T.
 
     q, k: [B, H, T, dk]; v: [B, H, T, dv]; f: [B, H, T] (any float dtype, used
@@ -39,6 +39,12 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     chunk_states) with the optional members None unless requested;
     chunk_states [B, H, ceil(T/64), dk, dv] bf16 holds the state entering each
     64-step chunk (bf16 path only).
+
+    resume=True (bf16 only): the previous call on this device and stream was a
+    forward of the same k, v, f made without save_states (typically state-only,
+    want_output=False); this call reuses its chunk-local states and runs only
+    the carry from `initial_state` and the output pass
+    (mogt_gated_scan_fwd_resume).
     """
     _require_cuda(q, k, v, f, initial_state, what="gated_scan")
     if k.ndim != 4 or v.ndim != 4 or f.ndim != 3 or (q is not None and q.ndim != 4):
@@ -78,11 +84,14 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     with torch.cuda.device(dev):
         w = N.workspaces.entry(dev, nbytes, "gated_fwd")
         ws = w.buf
-        st = L.mogt_gated_scan_fwd(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o), N.ptr(S0),
-                                   N.ptr(S_fin), N.ptr(dec), N.ptr(seg), BH, T, dk, dv, icode, ocode,
-                                   N.ptr(ws), ws.numel(), N.stream_ptr(dev))
-        N.check(st, "mogt_gated_scan_fwd")
-        w.after_launch("mogt_gated_scan_fwd")
+        if resume and in_dtype != torch.bfloat16:
+            raise ValueError("resume needs bf16 inputs")
+        fn = L.mogt_gated_scan_fwd_resume if resume else L.mogt_gated_scan_fwd
+        name = "mogt_gated_scan_fwd_resume" if resume else "mogt_gated_scan_fwd"
+        st = fn(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o), N.ptr(S0), N.ptr(S_fin), N.ptr(dec),
+                N.ptr(seg), BH, T, dk, dv, icode, ocode, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
+        N.check(st, name)
+        w.after_launch(name)
     return o, S_fin, dec, seg
 
 

@@ -12,8 +12,11 @@ carries of the reference (affine_scan.py:250-271).  So:
      [world, B, H, 1 + dk*dv] fp32 tensor, ~197 KB per rank at H=12, 64x64);
   3. rank r combines the carries of ranks < r into its incoming state
      X_r = A_{r-1} X_{r-1} + S_{r-1} (X_0 = initial state or 0);
-  4. every rank runs the full forward on its segment from X_r: this is the
+  4. every rank runs the output pass on its segment from X_r: this is the
      local correction pass that makes its outputs equal to a one-GPU scan.
+     On the CUDA path it resumes the forward of step 1 (the chunk-local states
+     are still in the workspace), so only the segment carry and the output
+     kernel run again.
 """
 from __future__ import annotations
 
@@ -67,5 +70,8 @@ def gated_scan_sp(q, k, v, f, *, group=None, output_dtype=None, initial_state=No
     gathered = flat.view((world,) + tuple(carry.shape))
     X = combine_carries(gathered, rank, dk, dv, initial_state)
     with torch.autograd.profiler.record_function("mogt.sp.local_scan"):
-        o, _, _, _ = fwd(q, k, v, f, initial_state=X, output_dtype=output_dtype)
+        if local_fwd is None and k.dtype == torch.bfloat16:
+            o, _, _, _ = fwd(q, k, v, f, initial_state=X, output_dtype=output_dtype, resume=True)
+        else:
+            o, _, _, _ = fwd(q, k, v, f, initial_state=X, output_dtype=output_dtype)
     return o

@@ -156,3 +156,24 @@ def test_every_output_row_written(mg, H, T):
     assert torch.isfinite(o).all()
     ref = O.gated_scan(*as64(q, k, v, f))
     assert rel_max_err(o.cpu().numpy(), ref) <= TOL_BF16
+
+
+@pytest.mark.parametrize("T", [700, 9000])
+def test_resume_after_state_only_pass(mg, T):
+    """mogt_gated_scan_fwd_resume (the sequence-parallel scan's second pass):
+    a state-only forward, then the output pass resumed from an initial state,
+    equals one forward from that state, and its final state and decay equal
+    the state-only pass's carried through that state."""
+    from mogt_b200 import ops
+    q, k, v, f = (t.cuda() for t in headed_bf16(2, 3, T, seed=11 + T))
+    S0 = torch.randn(2, 3, 64, 64, generator=torch.Generator().manual_seed(T)).cuda()
+    _, S_loc, A_loc, _ = ops.gated_scan_fwd(None, k, v, f, want_final=True, want_output=False)
+    o_r, S_r, A_r, _ = ops.gated_scan_fwd(q, k, v, f, initial_state=S0, want_final=True, resume=True)
+    o_f, S_f, A_f, _ = ops.gated_scan_fwd(q, k, v, f, initial_state=S0, want_final=True)
+    assert rel_max_err(o_r.float().cpu().numpy(), o_f.float().cpu().numpy()) <= 1e-2
+    assert torch.allclose(A_r, A_f) and torch.allclose(A_loc, A_f)
+    carried = A_loc[..., None, None] * S0 + S_loc
+    assert rel_max_err(S_r.cpu().numpy(), carried.cpu().numpy()) <= 1e-4
+    assert rel_max_err(S_r.cpu().numpy(), S_f.cpu().numpy()) <= 1e-5
+    ref = O.gated_scan(*as64(q, k, v, f), S0=as64(S0)[0])
+    assert rel_max_err(o_r.float().cpu().numpy(), ref) <= TOL_BF16
