@@ -536,8 +536,8 @@ def extra_sp(dev, world, rank):
     torch.cuda.empty_cache()
     return {"ms": ms, "tokens_per_s": T / (ms / 1e3), "T": T, "ranks": world,
             "rel_max_err_vs_one_gpu_scan": err,
-            "note": "state-only segment scan + NCCL all-gather of (decay, state) carries + local scan; "
-                    "outputs bf16 on both sides"}
+            "note": "state-only segment scan + NCCL all-gather of (decay, state) carries + the forward "
+                    "resumed from the incoming state (carry + output pass); outputs bf16 on both sides"}
 
 
 def _time_call(call, n, warm=2):
