@@ -459,6 +459,12 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
     lam_cur = __ldg(p.lam + u);
   }
   const int t0 = 16 * warp + g, t1 = t0 + 8;   // this thread's rows of a chunk
+  // this thread's stmatrix / ldmatrix row offsets in a 64x64 tile, per (half, x4)
+  uint32_t fro[2][2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+#pragma unroll
+    for (int x = 0; x < 2; ++x) fro[h][x] = frag_row_addr(0u, warp, lane, h, x);
   // (head, chunk, segment) of the current item, stepped backwards without divisions
   int bh = 0, c = 0, seg = 0;
   if (n > 0) {
@@ -516,7 +522,7 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
       for (int h = 0; h < 2; ++h)
 #pragma unroll
         for (int x = 0; x < 2; ++x) {
-          const uint32_t addr = frag_row_addr(lt, warp, lane, h, x);
+          const uint32_t addr = lt + fro[h][x];
           uint32_t r[4];
           ldsm_x4_v(r, addr);
           frag_unpack(sv, h, x, r);
@@ -598,7 +604,7 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
         for (int x = 0; x < 2; ++x) {
           uint32_t r[4];
           frag_pack(r, pr, h, x);
-          stsm_x4(frag_row_addr(kt, warp, lane, h, x), r);
+          stsm_x4(kt + fro[h][x], r);
         }
     }
     fence_proxy_async();
@@ -663,7 +669,7 @@ __global__ void __launch_bounds__(B_THREADS, B_CTAS_PER_SM)
           for (int x = 0; x < 2; ++x) {
             uint32_t r[4];
             frag_pack(r, ov, h, x);
-            stsm_x4(frag_row_addr(st, warp, lane, h, x), r);
+            stsm_x4(st + fro[h][x], r);
           }
         fence_proxy_async();
         __syncwarp();
