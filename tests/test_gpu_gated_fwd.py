@@ -177,3 +177,26 @@ def test_resume_after_state_only_pass(mg, T):
     assert rel_max_err(S_r.cpu().numpy(), S_f.cpu().numpy()) <= 1e-5
     ref = O.gated_scan(*as64(q, k, v, f), S0=as64(S0)[0])
     assert rel_max_err(o_r.float().cpu().numpy(), ref) <= TOL_BF16
+
+
+def test_mixed_gates_across_multi_chunk_segments(mg):
+    """Exact-decay chunks (zero, one and tiny gates) inside segments of several
+    chunks (BH = 2, T = 65536: five chunks per segment of the local pass),
+    with an initial state: outputs, final state and decay, and the saved
+    state entering sampled chunks, against the float64 oracle."""
+    m, _ = mg
+    T = 65536
+    q, k, v, f = headed_bf16(1, 2, T, seed=21, f_mode="mixed")
+    S0 = torch.randn(1, 2, 64, 64, generator=torch.Generator().manual_seed(3))
+    o, S_fin, dec, seg = m.ops.gated_scan_fwd(q.cuda(), k.cuda(), v.cuda(), f.cuda(),
+                                              initial_state=S0.cuda(), output_dtype=torch.float32,
+                                              want_final=True, save_states=True)
+    q64, k64, v64, f64 = as64(q, k, v, f)
+    ref, Sref = O.gated_scan(q64, k64, v64, f64, S0=S0.double().numpy(), return_final=True)
+    assert rel_max_err(o.cpu().numpy(), ref) <= TOL_BF16
+    assert rel_max_err(S_fin.cpu().numpy(), Sref) <= TOL_BF16
+    assert np.allclose(dec.cpu().numpy(), np.prod(f64, axis=-1), rtol=1e-3, atol=1e-30)
+    for c in (1, 5, 6, 333, 1023):
+        _, Sc = O.gated_scan(q64[:, :, :64 * c], k64[:, :, :64 * c], v64[:, :, :64 * c],
+                             f64[:, :, :64 * c], S0=S0.double().numpy(), return_final=True)
+        assert rel_max_err(seg[:, :, c].float().cpu().numpy(), Sc) <= TOL_BF16
