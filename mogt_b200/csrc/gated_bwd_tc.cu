@@ -39,6 +39,7 @@
 #include "common.cuh"
 #include "gated_common.cuh"
 #include "lookback.cuh"
+#include "gated_internal.h"
 
 namespace mogt {
 namespace gated {
@@ -98,6 +99,12 @@ struct Params {
   float* a_inc;
   float* st_agg;
   float* st_inc;
+  // when set: the carry entering every stripe's end comes from the segment
+  // passes (gated_bwd_seg_agg + the segment carry), [BH][nseg_b][4096] in the
+  // stripe-aggregate layout, segments in reverse time order; pass 1 and the
+  // look-back are skipped
+  const float* x_in;
+  int nseg_b, nsub;
   int T, BH, nchunks, cps, nstripes;
 };
 
@@ -170,7 +177,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int c_begin = stripe * p.cps;
   const int nc = min(p.cps, p.nchunks - c_begin);
   const bool has_succ = stripe > 0;   // an earlier stripe waits for this carry
-  const int n1 = has_succ ? nc : 0;
+  const int n1 = (has_succ && !p.x_in) ? nc : 0;
   const int nit = n1 + nc;
   const float* fh = p.f + (size_t)bh * T;
   uint32_t ph_a = 0, ph_b = 0, ph_c = 0, ph_d = 0, ph_e = 0;
@@ -324,6 +331,19 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   float a_in = 1.f;
   if (ci == 0) {
     zero44(X);
+  } else if (p.x_in) {
+    // the state of the reversed segment that follows this stripe's last one
+    const int g_last = (stripe + 1) * p.nsub - 1;
+    const float4* src = reinterpret_cast<const float4*>(
+        p.x_in + ((size_t)bh * p.nseg_b + (p.nseg_b - 1 - g_last)) * (D * D) + (size_t)tid * 16);
+#pragma unroll
+    for (int n = 0; n < 4; ++n) {
+      const float4 v = __ldcg(src + n);
+      X[n][0] = v.x;
+      X[n][1] = v.y;
+      X[n][2] = v.z;
+      X[n][3] = v.w;
+    }
   } else {
     LookbackBufs lb{p.flags, p.a_agg, p.a_inc, p.st_agg, p.st_inc, p.hdr};
     lookback_scalar_state<4>(X, a_in, lb, ci, (uint32_t)bh, (uint32_t)BH, epoch, unit,
@@ -708,6 +728,126 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   if (tid == 0) finish_cta(p.hdr, epoch, gridDim.x);
 }
 
+// ---------------------------------------------------------------------------
+// gated_bwd_seg_agg: the backward carry's aggregate over a segment of chunks
+// (a third of a stripe), sum_c exp2(lpre_c) (diag(exp2 l) Q_c)^T dO_c with
+// lpre_c the log2 decay of the segment's chunks before c, and the segment's
+// total log2 decay: the quantities pass 1 forms per stripe, here with three
+// light CTAs per SM and one accumulator in tensor memory.  Written in reverse
+// segment order, so that the forward's segment carry kernel run over them
+// gives the carry entering each segment's end from the later ones.
+// ---------------------------------------------------------------------------
+constexpr int AB_RS = 4;                      // (q, do) ring slots
+constexpr int AB_NBARS = 2 * AB_RS + 1;       // full and empty per slot, all-done
+constexpr int AB_SM_BAR = AB_RS * 2 * TILE;
+constexpr int AB_SM_TSLOT = AB_SM_BAR + 8 * AB_NBARS;
+constexpr int AB_SM_ALLOC = AB_SM_TSLOT + 16 + 1024;
+static_assert(3 * (AB_SM_ALLOC + 1024) <= 228 * 1024, "three CTAs per SM");
+
+struct AggParams {
+  const float* f;
+  float* agg;    // [BH][nseg][4096] reversed segment order, stripe-aggregate layout
+  float* lam;    // [BH][nseg]
+  WsHeader* hdr;
+  int T, BH, nchunks, cps, nsub, seg_len, nseg;
+};
+
+__global__ void __launch_bounds__(NTHREADS, 3)
+    gated_bwd_seg_agg(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tdo,
+                      const AggParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~uintptr_t(1023));
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int qd = warp & 3, hf = warp >> 2;
+  const int br0 = build_row(tid, 0), br1 = build_row(tid, 1);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + AB_SM_BAR);
+  uint64_t* empty = full + AB_RS;
+  uint64_t* done = full + 2 * AB_RS;
+  uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + AB_SM_TSLOT);
+  if (warp == 0) tmem_alloc(tslot, 64);
+  if (tid == 0) {
+#pragma unroll
+    for (int i = 0; i < AB_NBARS; ++i) mbar_init(&full[i], 1);
+    fence_barrier_init();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tbase = *tslot;
+  const uint32_t tw = tbase + ((uint32_t)(32 * qd) << 16) + 32u * hf;
+  const int gseg = blockIdx.x / p.BH, bh = blockIdx.x % p.BH;   // gseg in time order
+  const int stripe = gseg / p.nsub, j = gseg % p.nsub;
+  const int s0 = stripe * p.cps, s1 = min(s0 + p.cps, p.nchunks);
+  const int c0 = min(s0 + j * p.seg_len, s1), c1 = min(c0 + p.seg_len, s1);
+  const int n = c1 - c0, T = p.T;
+  const float* fh = p.f + (size_t)bh * T;
+  bool ok = true;
+
+  auto issue = [&](int i) {
+    if (i >= n) return;
+    const int slot = i % AB_RS;
+    uint8_t* base = smem + slot * 2 * TILE;
+    mbar_arrive_expect_tx(&full[slot], 2 * TILE);
+    tma_load_3d(base, &tq, &full[slot], 0, (c0 + i) * CH, bh);
+    tma_load_3d(base + TILE, &tdo, &full[slot], 0, (c0 + i) * CH, bh);
+  };
+  if (tid == 0)
+    for (int i = 0; i < AB_RS; ++i) issue(i);
+
+  float lrun = 0.f;
+  float2 fnext = n > 0 ? gate_load(fh, T, c0, lane) : make_float2(1.f, 1.f);
+  for (int i = 0; i < n; ++i) {
+    const WGates gt = warp_gates(fnext, lane);
+    if (i + 1 < n) fnext = gate_load(fh, T, c0 + i + 1, lane);
+    const int slot = i % AB_RS;
+    if (!mbar_wait(&full[slot], (i / AB_RS) & 1)) ok = false;
+    uint8_t* base = smem + slot * 2 * TILE;
+    // Q rows scaled in place by exp2(lpre + l_t) (every factor <= 1)
+    const float e0 = fast_exp2(lrun + gt.l0), e1 = fast_exp2(lrun + gt.l1);
+    build_rows(base, base, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
+    fence_proxy_async();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 0) {
+      tc_fence_after();
+      umma_64x64x64(tbase, smem_u32(base), true, smem_u32(base + TILE), true, i > 0);
+      umma_commit(&empty[slot]);
+      // the slot of chunk i-1 is free once its product completed
+      if (i >= 1 && i - 1 + AB_RS < n) {
+        const int ps = (i - 1) % AB_RS;
+        if (!mbar_wait(&empty[ps], ((i - 1) / AB_RS) & 1)) ok = false;
+        issue(i - 1 + AB_RS);
+      }
+    }
+    __syncwarp();
+    lrun += gt.tot;
+  }
+  float acc[4][4];
+  zero44(acc);
+  if (n > 0) {
+    if (tid == 0) umma_commit(done);
+    __syncwarp();
+    if (!mbar_wait(done, 0)) ok = false;
+    __syncwarp();
+    tc_fence_after();
+    tmem_ld_16x32(acc, tw);
+    tc_fence_before();
+  }
+  const size_t gi = (size_t)bh * p.nseg + (p.nseg - 1 - gseg);
+  float4* dst = reinterpret_cast<float4*>(p.agg + gi * (D * D) + (size_t)tid * 16);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) __stcg(dst + k, make_float4(acc[k][0], acc[k][1], acc[k][2], acc[k][3]));
+  if (tid == 0) p.lam[gi] = lrun;
+  if (!ok) record_error(p.hdr, MOGT_ERR_TIMEOUT, blockIdx.x);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tbase, 64);
+  }
+}
+
 }  // namespace bwd
 }  // namespace gated
 }  // namespace mogt
@@ -719,9 +859,27 @@ using namespace mogt::gated;
 namespace mogt {
 namespace gated {
 
+// The stripe kernel's look-back workspace, then the segment aggregates, log2
+// decays and carries of the segment passes (bwd::kSub segments per stripe).
+namespace bwd {
+constexpr int kSub = 3;
+struct SegLayout {
+  size_t agg, lam, state, total;
+};
+inline SegLayout seg_layout(size_t base, size_t BH, size_t nseg) {
+  SegLayout l;
+  l.agg = mogt_host::align_up(base, 256);
+  l.lam = l.agg + BH * nseg * D * D * 4;
+  l.state = l.lam + mogt_host::align_up(BH * nseg * 4, 256);
+  l.total = l.state + BH * nseg * D * D * 4;
+  return l;
+}
+}  // namespace bwd
+
 size_t bwd_tc_workspace_bytes(int64_t BH, int64_t T) {
   const Plan pl = make_plan(BH, T, sm_count());
-  return ws_layout((size_t)BH * pl.nstripes).total;
+  const size_t base = ws_layout((size_t)BH * pl.nstripes).total;
+  return bwd::seg_layout(base, (size_t)BH, (size_t)pl.nstripes * bwd::kSub).total;
 }
 
 // Tensor-core backward; arguments are checked by the caller.
@@ -732,7 +890,9 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   const size_t NU = (size_t)BH * pl.nstripes;
   if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
   const WsLayout L = ws_layout(NU);
-  if (!workspace || workspace_bytes < L.total) return MOGT_ERR_WORKSPACE;
+  const int nseg = pl.nstripes * bwd::kSub;
+  const bwd::SegLayout SL = bwd::seg_layout(L.total, (size_t)BH, (size_t)nseg);
+  if (!workspace || workspace_bytes < SL.total) return MOGT_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOGT_ERR_ALIGN;
   CUtensorMap maps[8];
   const void* srcs[8] = {q, k, v, d_o, chunk_states, dq, dk, dv};
@@ -765,6 +925,30 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   P.nchunks = pl.nchunks;
   P.cps = pl.cps;
   P.nstripes = pl.nstripes;
+  // the carry entering every stripe's end: segment aggregates (three light
+  // CTAs per SM) and the segment carry, instead of the stripe kernel's pass 1
+  // and look-back
+  bwd::AggParams A;
+  A.f = f;
+  A.agg = reinterpret_cast<float*>(ws + SL.agg);
+  A.lam = reinterpret_cast<float*>(ws + SL.lam);
+  A.hdr = P.hdr;
+  A.T = T;
+  A.BH = BH;
+  A.nchunks = pl.nchunks;
+  A.cps = pl.cps;
+  A.nsub = bwd::kSub;
+  A.seg_len = (pl.cps + bwd::kSub - 1) / bwd::kSub;
+  A.nseg = nseg;
+  cudaFuncSetAttribute(bwd::gated_bwd_seg_agg, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                       bwd::AB_SM_ALLOC);
+  bwd::gated_bwd_seg_agg<<<(unsigned)((size_t)BH * nseg), NTHREADS, bwd::AB_SM_ALLOC, s>>>(maps[0], maps[3], A);
+  float* xstate = reinterpret_cast<float*>(ws + SL.state);
+  const int cs = launch_seg_carry(A.agg, A.lam, xstate, BH, nseg, s);
+  if (cs != MOGT_OK) return cs;
+  P.x_in = xstate;
+  P.nseg_b = nseg;
+  P.nsub = bwd::kSub;
   cudaFuncSetAttribute(bwd::gated_bwd_stripe, cudaFuncAttributeMaxDynamicSharedMemorySize,
                        bwd::SM_ALLOC);
   bwd::gated_bwd_stripe<<<(unsigned)NU, NTHREADS, bwd::SM_ALLOC, s>>>(

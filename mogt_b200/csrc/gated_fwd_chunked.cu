@@ -746,6 +746,13 @@ size_t chunked_fwd_workspace_bytes(int64_t BH, int64_t T) {
   return chunked::layout((size_t)BH, pl).total;
 }
 
+int launch_seg_carry(const float* agg, const float* lam, float* state, int64_t BH, int nseg,
+                     cudaStream_t s) {
+  chunked::gated_seg_carry<<<dim3(D * D / 32, (unsigned)BH), 32 * chunked::C_WARPS, 0, s>>>(
+      agg, lam, state, nullptr, nullptr, nullptr, nseg);
+  return mogt_host::launch_status();
+}
+
 int launch_chunked_fwd(const void* q, const void* k, const void* v, const float* f, void* o,
                        const float* S0, float* S_final, float* decay_final, void* chunk_states,
                        int64_t BH, int64_t T, int out_dtype, void* workspace,
