@@ -26,19 +26,20 @@
 // Every decay is formed per element from differences of l, so the form is
 // exact for any gates (no factorisation condition, no fallback path).
 //
-// Work decomposition mirrors the forward: the chunks of a head are cut into
-// stripes; a CTA (8 warps, one per SM) owns a stripe and runs
-//   pass 1  the stripe's carry aggregate  sum_c exp2(lpre_c) Q^_c^T dO_c
-//           (lpre = log2 decay of the stripe's chunks before c) in tensor
-//           memory, published for the stripe before it;
-//   look-back  over the later stripes of the head (windowed, decoupled) for
-//           the carry entering the stripe's end;
-//   pass 2  the chunks in reverse order: 9 tcgen05 MMAs per chunk (6 of the
-//           carry and the raw tiles, 3 of the masked products), epilogues
-//           in registers, and one warp forms df from per-step partial sums.
+// Work decomposition: the chunks of a head are cut into stripes, each stripe
+// into kSub segments.
+//   gated_bwd_seg_agg  (three light CTAs per SM) every segment's carry
+//           aggregate  sum_c exp2(lpre_c) Q^_c^T dO_c  (lpre = log2 decay of
+//           the segment's chunks before c) and log2 decay, in reverse order;
+//   the forward's segment carry kernel composes them into the carry entering
+//           every segment's end from the later ones;
+//   gated_bwd_stripe  (8 warps, one CTA per SM) per stripe, from the carry
+//           entering its end, the chunks in reverse order: 9 tcgen05 MMAs
+//           per chunk (6 of the carry and the raw tiles, 3 of the masked
+//           products), epilogues in registers, and one warp forms df from
+//           per-step partial sums.
 #include "common.cuh"
 #include "gated_common.cuh"
-#include "lookback.cuh"
 #include "gated_internal.h"
 
 namespace mogt {
@@ -46,8 +47,6 @@ namespace gated {
 namespace bwd {
 
 constexpr int STAGES = 3;                  // pass-2 ring: q, k, v, do, S_in per slot
-constexpr int P1_STAGES = 7;               // pass-1 ring: q, do per slot
-constexpr int P1_AHEAD = 3;                // chunks c+3, c+4 load into the slots of pair c/2 - 2
 constexpr int SLOT = 5 * TILE;
 constexpr int T_Q = 0, T_K = 1, T_V = 2, T_DO = 3, T_S = 4;
 
@@ -60,30 +59,28 @@ constexpr int SM_PQ = SM_M1 + TILE;                // PQd, [u][s]
 constexpr int SM_OUT = SM_PQ + TILE;               // dq, dk, dv staging tiles [3] (TMA stores)
 constexpr int SM_GL = SM_OUT + 3 * TILE;           // l_t of the chunk [64]
 constexpr int SM_GW = SM_GL + 256;                 // w_t [64]
-constexpr int SM_LPRE = SM_GW + 256;               // pass-1 prefix decays [MAX_CPS]
 // per-chunk partial sums for df, double-buffered by chunk parity (df of chunk
 // j is formed during chunk j+1)
 constexpr int PART = 512 * 3 + 1024 + 256 + 64;    // one parity's partials
-constexpr int SM_ROWZ = SM_LPRE + MAX_CPS * 4;     // [2][64] halves of z_u
+constexpr int SM_ROWZ = SM_GW + 256;               // [2][64] halves of z_u
 constexpr int SM_ROWY = SM_ROWZ + 512;             // [2][64] halves of y_s
 constexpr int SM_ROWK = SM_ROWY + 512;             // [2][64] halves of k.(M1d^T Q)
 constexpr int SM_COLW = SM_ROWK + 512;             // [4][64] column sums of the E prefix
 constexpr int SM_ROWT = SM_COLW + 1024;            // [64] row totals of E, columns 0..31
 constexpr int SM_SIG = SM_ROWT + 256;              // [8] <X, S_in> per warp
 constexpr int SM_MISC = SM_ROWZ + 2 * PART;        // ticket, look-back scratch
-constexpr int NBARS = STAGES + P1_STAGES + 2 + 5;
+constexpr int NBARS = STAGES + 5;
 constexpr int SM_BAR = SM_MISC + 256;
 constexpr int SM_TSLOT = SM_BAR + 8 * NBARS;
 constexpr int SM_TOTAL = SM_TSLOT + 16;
 constexpr int SM_ALLOC = SM_TOTAL + 1024;
 static_assert(SM_ALLOC <= 227 * 1024, "shared memory per CTA");
-static_assert(P1_STAGES * 2 * TILE <= SM_QH - SM_RING, "pass-1 ring fits");
 
 // tensor memory (fp32 M = 64 accumulators): group-1 products, then the
 // group-2 products reuse the M1 / PQ columns once those are read
 constexpr uint32_t TMEM_COLS = 512;
 constexpr uint32_t TM_M1 = 0, TM_PQ = 64, TM_DOS = 128, TM_DX = 192, TM_VX = 256, TM_KX = 320,
-                   TM_DV2 = 384, TM_AGG = 448;
+                   TM_DV2 = 384;
 constexpr uint32_t TM_DQ2 = TM_M1, TM_DK2 = TM_PQ;
 
 struct Params {
@@ -94,11 +91,6 @@ struct Params {
   float* df;
   float* dS0;
   WsHeader* hdr;
-  uint32_t* flags;
-  float* a_agg;
-  float* a_inc;
-  float* st_agg;
-  float* st_inc;
   // when set: the carry entering every stripe's end comes from the segment
   // passes (gated_bwd_seg_agg + the segment carry), [BH][nseg_b][4096] in the
   // stripe-aggregate layout, segments in reverse time order; pass 1 and the
@@ -137,17 +129,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int br0 = build_row(tid, 0), br1 = build_row(tid, 1);
   float* sgl = reinterpret_cast<float*>(smem + SM_GL);
   float* sgw = reinterpret_cast<float*>(smem + SM_GW);
-  float* lpre = reinterpret_cast<float*>(smem + SM_LPRE);
   auto part = [&](int off, int par) { return reinterpret_cast<float*>(smem + off + par * PART); };
   volatile uint32_t* bc = reinterpret_cast<volatile uint32_t*>(smem + SM_MISC);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SM_BAR);
-  uint64_t* bars1 = bars + STAGES;
-  uint64_t* bar_k = bars1 + P1_STAGES;      // pass-1 MMA commits (2)
-  uint64_t* bar_a = bar_k + 2;              // M1, PQ
-  uint64_t* bar_b = bar_k + 3;              // dO S_in^T, Q^^T dO
-  uint64_t* bar_c = bar_k + 4;              // V X^T, K X
-  uint64_t* bar_d = bar_k + 5;              // M1d (w K)
-  uint64_t* bar_e = bar_k + 6;              // M1d^T Q, PQd^T dO
+  uint64_t* bar_a = bars + STAGES;          // M1, PQ
+  uint64_t* bar_b = bar_a + 1;              // dO S_in^T, Q^^T dO
+  uint64_t* bar_c = bar_a + 2;              // V X^T, K X
+  uint64_t* bar_d = bar_a + 3;              // M1d (w K)
+  uint64_t* bar_e = bar_a + 4;              // M1d^T Q, PQd^T dO
   uint32_t* tslot = reinterpret_cast<uint32_t*>(smem + SM_TSLOT);
   uint8_t* qh_tile = smem + SM_QH;
   uint8_t* kw_tile = smem + SM_KW;
@@ -176,163 +165,43 @@ __global__ void __launch_bounds__(NTHREADS, 1)
   const int stripe = p.nstripes - 1 - ci;
   const int c_begin = stripe * p.cps;
   const int nc = min(p.cps, p.nchunks - c_begin);
-  const bool has_succ = stripe > 0;   // an earlier stripe waits for this carry
-  const int n1 = (has_succ && !p.x_in) ? nc : 0;
-  const int nit = n1 + nc;
+  const int nit = nc;
   const float* fh = p.f + (size_t)bh * T;
   uint32_t ph_a = 0, ph_b = 0, ph_c = 0, ph_d = 0, ph_e = 0;
   bool ok = true;
 
-  uint64_t pol_keep = 0, pol_stream = 0;
-  if (tid == 0) {
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(pol_keep));
+  uint64_t pol_stream = 0;
+  if (tid == 0)
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol_stream));
-  }
-  // TMA loads of pipeline iteration `it`: pass 1 chunks c_begin.. forward
-  // (q, do), then pass 2 chunks in reverse (q, k, v, do, S_in)
+  // TMA loads of pipeline iteration `it`: the stripe's chunks in reverse
+  // (q, k, v, do, S_in)
   auto issue = [&](int it) {
     if (it >= nit) return;
-    if (it < n1) {
-      const int t0 = (c_begin + it) * CH;
-      const int slot = it % P1_STAGES;
-      uint8_t* base = smem + SM_RING + slot * 2 * TILE;
-      mbar_arrive_expect_tx(&bars1[slot], 2 * TILE);
-      tma_load_3d_hint(base, &tq, &bars1[slot], 0, t0, bh, pol_keep);
-      tma_load_3d_hint(base + TILE, &tdo, &bars1[slot], 0, t0, bh, pol_keep);
-    } else {
-      const int j = it - n1, slot = j % STAGES;
-      const int gc = c_begin + nc - 1 - j, t0 = gc * CH;
-      uint8_t* base = smem + SM_RING + slot * SLOT;
-      mbar_arrive_expect_tx(&bars[slot], 5 * TILE);
-      tma_load_3d_hint(base + T_Q * TILE, &tq, &bars[slot], 0, t0, bh, pol_stream);
-      tma_load_3d_hint(base + T_K * TILE, &tk, &bars[slot], 0, t0, bh, pol_stream);
-      tma_load_3d_hint(base + T_V * TILE, &tv, &bars[slot], 0, t0, bh, pol_stream);
-      tma_load_3d_hint(base + T_DO * TILE, &tdo, &bars[slot], 0, t0, bh, pol_stream);
-      tma_load_3d_hint(base + T_S * TILE, &ts, &bars[slot], 0, t0, bh, pol_stream);
-    }
+    const int slot = it % STAGES;
+    const int gc = c_begin + nc - 1 - it, t0 = gc * CH;
+    uint8_t* base = smem + SM_RING + slot * SLOT;
+    mbar_arrive_expect_tx(&bars[slot], 5 * TILE);
+    tma_load_3d_hint(base + T_Q * TILE, &tq, &bars[slot], 0, t0, bh, pol_stream);
+    tma_load_3d_hint(base + T_K * TILE, &tk, &bars[slot], 0, t0, bh, pol_stream);
+    tma_load_3d_hint(base + T_V * TILE, &tv, &bars[slot], 0, t0, bh, pol_stream);
+    tma_load_3d_hint(base + T_DO * TILE, &tdo, &bars[slot], 0, t0, bh, pol_stream);
+    tma_load_3d_hint(base + T_S * TILE, &ts, &bars[slot], 0, t0, bh, pol_stream);
   };
   auto wait_bar = [&](uint64_t* bar, uint32_t& ph) {
     if (!mbar_wait(bar, ph)) ok = false;
     ph ^= 1u;
   };
 
-  if (tid == 0) {
-    if (n1 > 0)
-      for (int it = 0; it < P1_AHEAD && it < n1; ++it) issue(it);
-    else
-      for (int it = 0; it < STAGES - 1; ++it) issue(it);
-  }
-
-  // ---------------- pass 1: the stripe's carry aggregate ----------------
-  float agg[4][4];
-  zero44(agg);
-  float ltot = 0.f;
-  if (n1 > 0) {
-    // lpre[c] = log2 decay of the stripe's chunks before c
-    for (int c = warp; c < n1; c += NTHREADS / 32) {
-      const float2 fv = gate_load(fh, T, c_begin + c, lane);
-      float x = clamped_log2(fv.x) + clamped_log2(fv.y);
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-      if (lane == 0) lpre[c] = x;
-    }
-    __syncthreads();
-    if (warp == 0) {
-      const int per = (n1 + 31) / 32, c0 = lane * per, c1 = min(c0 + per, n1);
-      float part = 0.f;
-      for (int c = c0; c < c1; ++c) part += lpre[c];
-      float inc = part;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const float y = __shfl_up_sync(0xffffffffu, inc, o);
-        if (lane >= o) inc += y;
-      }
-      if (lane == 31) bc[2] = __float_as_uint(inc);
-      float run = inc - part;
-      for (int c = c0; c < c1; ++c) {
-        const float x = lpre[c];
-        lpre[c] = run;
-        run += x;
-      }
-    }
-    __syncthreads();
-    // chunks in pairs: two scaled tiles per CTA barrier, the pair's MMAs
-    // committed together; tile sets alternate between pairs
-    const int np = (n1 + 1) / 2;
-    float2 fa = gate_load(fh, T, c_begin, lane);
-    float2 fb = n1 > 1 ? gate_load(fh, T, c_begin + 1, lane) : make_float2(1.f, 1.f);
-    for (int pi = 0; pi < np; ++pi) {
-      const int c = 2 * pi;
-      const bool two = c + 1 < n1;
-      const WGates ga = warp_gates(fa, lane), gb = warp_gates(fb, lane);
-      if (c + 2 < n1) fa = gate_load(fh, T, c_begin + c + 2, lane);
-      if (c + 3 < n1) fb = gate_load(fh, T, c_begin + c + 3, lane);
-      if (pi >= 2) {
-        const uint32_t ph = ((pi - 2) >> 1) & 1;
-        if (!mbar_wait(&bar_k[pi & 1], ph)) ok = false;   // MMAs of pair pi-2 done
-      }
-      if (tid == 0) {   // into the slots of pair pi-2
-        if (c + P1_AHEAD < n1) issue(c + P1_AHEAD);
-        if (c + 1 + P1_AHEAD < n1) issue(c + 1 + P1_AHEAD);
-      }
-      uint8_t* t0 = (pi & 1) ? x_tile : qh_tile;
-      uint8_t* t1 = (pi & 1) ? m1_tile : kw_tile;
-      uint8_t* base0 = smem + SM_RING + (c % P1_STAGES) * 2 * TILE;
-      uint8_t* base1 = smem + SM_RING + ((c + 1) % P1_STAGES) * 2 * TILE;
-      if (!mbar_wait(&bars1[c % P1_STAGES], (c / P1_STAGES) & 1)) ok = false;
-      {
-        const float sc = lpre[c];
-        const float e0 = fast_exp2(sc + ga.l0), e1 = fast_exp2(sc + ga.l1);
-        build_rows(t0, base0, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
-      }
-      if (two) {
-        if (!mbar_wait(&bars1[(c + 1) % P1_STAGES], ((c + 1) / P1_STAGES) & 1)) ok = false;
-        const float sc = lpre[c + 1];
-        const float e0 = fast_exp2(sc + gb.l0), e1 = fast_exp2(sc + gb.l1);
-        build_rows(t1, base1, step_val(e0, e1, br0), step_val(e0, e1, br1), tid);
-      }
-      fence_proxy_async();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-        umma_64x64x64(tbase + TM_AGG, smem_u32(t0), true, smem_u32(base0 + TILE), true, c > 0);
-        if (two) umma_64x64x64(tbase + TM_AGG, smem_u32(t1), true, smem_u32(base1 + TILE), true, true);
-        umma_commit(&bar_k[pi & 1]);
-      }
-      __syncwarp();
-    }
-    {
-      const uint32_t ph = ((np - 1) >> 1) & 1;
-      if (!mbar_wait(&bar_k[(np - 1) & 1], ph)) ok = false;
-    }
-    tc_fence_after();
-    tmem_ld_16x32(agg, tw + TM_AGG);
-    tc_fence_before();
-    ltot = __uint_as_float(bc[2]);
-    __syncthreads();  // pass 1 has released the ring
-    if (tid == 0)
-      for (int it = n1; it < n1 + STAGES - 1; ++it) issue(it);
-  }
-  const float A_agg = fast_exp2(ltot);
-  const size_t st_off = (size_t)unit * (D * D) + (size_t)tid * 16;
-  if (n1 > 0 && ci > 0) {
-    float4* dst = reinterpret_cast<float4*>(p.st_agg + st_off);
-#pragma unroll
-    for (int n = 0; n < 4; ++n) __stcg(dst + n, make_float4(agg[n][0], agg[n][1], agg[n][2], agg[n][3]));
-    if (tid == 0) __stcg(p.a_agg + unit, A_agg);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release_u32(p.flags + unit, flag_tag(epoch, kFlagAgg));
-  }
+  if (tid == 0)
+    for (int it = 0; it < STAGES - 1; ++it) issue(it);
 
   // ---------------- carry entering the stripe's end ----------------
+  // from the segment passes: the state of the reversed segment that follows
+  // this stripe's last one (zero for the last stripe)
   float X[4][4];
-  float a_in = 1.f;
   if (ci == 0) {
     zero44(X);
-  } else if (p.x_in) {
-    // the state of the reversed segment that follows this stripe's last one
+  } else {
     const int g_last = (stripe + 1) * p.nsub - 1;
     const float4* src = reinterpret_cast<const float4*>(
         p.x_in + ((size_t)bh * p.nseg_b + (p.nseg_b - 1 - g_last)) * (D * D) + (size_t)tid * 16);
@@ -344,22 +213,6 @@ __global__ void __launch_bounds__(NTHREADS, 1)
       X[n][2] = v.z;
       X[n][3] = v.w;
     }
-  } else {
-    LookbackBufs lb{p.flags, p.a_agg, p.a_inc, p.st_agg, p.st_inc, p.hdr};
-    lookback_scalar_state<4>(X, a_in, lb, ci, (uint32_t)bh, (uint32_t)BH, epoch, unit,
-                             reinterpret_cast<float*>(smem + SM_MISC + 64),
-                             reinterpret_cast<volatile uint32_t*>(smem + SM_MISC + 16));
-  }
-  if (n1 > 0) {
-    float4* dst = reinterpret_cast<float4*>(p.st_inc + st_off);
-#pragma unroll
-    for (int n = 0; n < 4; ++n)
-      __stcg(dst + n, make_float4(fmaf(A_agg, X[n][0], agg[n][0]), fmaf(A_agg, X[n][1], agg[n][1]),
-                                  fmaf(A_agg, X[n][2], agg[n][2]), fmaf(A_agg, X[n][3], agg[n][3])));
-    if (tid == 0) __stcg(p.a_inc + unit, A_agg * a_in);
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) st_release_u32(p.flags + unit, flag_tag(epoch, kFlagInc));
   }
 
   // ---------------- pass 2: chunks in reverse ----------------
@@ -495,7 +348,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         umma_64x64x64(tbase + TM_KX, kb, false, smem_u32(x_tile), true, false);   // K X
         umma_commit(bar_c);
       } else if (warp == 3 && lane == 0) {
-        issue(n1 + j + STAGES - 1);  // into the slot of chunk j-1, released at the barrier
+        issue(j + STAGES - 1);  // into the slot of chunk j-1, released at the barrier
       }
       __syncwarp();
     }
@@ -878,7 +731,7 @@ inline SegLayout seg_layout(size_t base, size_t BH, size_t nseg) {
 
 size_t bwd_tc_workspace_bytes(int64_t BH, int64_t T) {
   const Plan pl = make_plan(BH, T, sm_count());
-  const size_t base = ws_layout((size_t)BH * pl.nstripes).total;
+  const size_t base = sizeof(WsHeader);
   return bwd::seg_layout(base, (size_t)BH, (size_t)pl.nstripes * bwd::kSub).total;
 }
 
@@ -889,9 +742,8 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   const Plan pl = make_plan(BH, T, sm_count());
   const size_t NU = (size_t)BH * pl.nstripes;
   if (NU >= ((size_t)1 << 31)) return MOGT_ERR_UNSUPPORTED;
-  const WsLayout L = ws_layout(NU);
   const int nseg = pl.nstripes * bwd::kSub;
-  const bwd::SegLayout SL = bwd::seg_layout(L.total, (size_t)BH, (size_t)nseg);
+  const bwd::SegLayout SL = bwd::seg_layout(sizeof(WsHeader), (size_t)BH, (size_t)nseg);
   if (!workspace || workspace_bytes < SL.total) return MOGT_ERR_WORKSPACE;
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) return MOGT_ERR_ALIGN;
   CUtensorMap maps[8];
@@ -915,11 +767,6 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   P.df = df;
   P.dS0 = dS0;
   P.hdr = reinterpret_cast<WsHeader*>(ws);
-  P.flags = reinterpret_cast<uint32_t*>(ws + L.flags);
-  P.a_agg = reinterpret_cast<float*>(ws + L.a_agg);
-  P.a_inc = reinterpret_cast<float*>(ws + L.a_inc);
-  P.st_agg = reinterpret_cast<float*>(ws + L.st_agg);
-  P.st_inc = reinterpret_cast<float*>(ws + L.st_inc);
   P.T = T;
   P.BH = BH;
   P.nchunks = pl.nchunks;
