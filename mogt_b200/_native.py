@@ -128,13 +128,14 @@ def _raise_timeout(what, unit):
 
 
 class _Workspace:
-    __slots__ = ("buf", "slot", "event", "what")
+    __slots__ = ("buf", "slot", "event", "what", "tag")
 
     def __init__(self, buf):
         self.buf = buf
         self.slot = torch.zeros(2, dtype=torch.int32).pin_memory()
         self.event = None
         self.what = None
+        self.tag = None   # what the last call left in the buffer (see ops.gated_scan_fwd)
 
     def clear_error(self):
         self.buf[12:20].zero_()

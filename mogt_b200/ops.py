@@ -47,6 +47,7 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
     (mogt_gated_scan_fwd_resume).
     """
     _require_cuda(q, k, v, f, initial_state, what="gated_scan")
+    src_ptrs = (k.data_ptr(), v.data_ptr(), f.data_ptr())   # the caller's tensors, before any copy
     if k.ndim != 4 or v.ndim != 4 or f.ndim != 3 or (q is not None and q.ndim != 4):
         raise ValueError("q, k, v must be [B, H, T, d] and f must be [B, H, T]")
     B, H, T, dk = k.shape
@@ -86,12 +87,19 @@ def gated_scan_fwd(q, k, v, f, *, initial_state=None, output_dtype=None, want_fi
         ws = w.buf
         if resume and in_dtype != torch.bfloat16:
             raise ValueError("resume needs bf16 inputs")
+        # the chunk-local states a resumed call reuses are those of the last
+        # forward on this workspace: same k, v, f, made without save_states
+        tag = ("gated_fwd_local",) + src_ptrs + (BH, T, dk, dv)
+        if resume and w.tag != tag:
+            raise ValueError("resume=True needs the previous forward on this device and stream to be "
+                             "a bf16 call with the same k, v, f made without save_states")
         fn = L.mogt_gated_scan_fwd_resume if resume else L.mogt_gated_scan_fwd
         name = "mogt_gated_scan_fwd_resume" if resume else "mogt_gated_scan_fwd"
         st = fn(N.ptr(q), N.ptr(k), N.ptr(v), N.ptr(f), N.ptr(o), N.ptr(S0), N.ptr(S_fin), N.ptr(dec),
                 N.ptr(seg), BH, T, dk, dv, icode, ocode, N.ptr(ws), ws.numel(), N.stream_ptr(dev))
         N.check(st, name)
         w.after_launch(name)
+        w.tag = tag if (in_dtype == torch.bfloat16 and seg is None) else None
     return o, S_fin, dec, seg
 
 

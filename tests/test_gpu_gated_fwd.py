@@ -200,3 +200,20 @@ def test_mixed_gates_across_multi_chunk_segments(mg):
         _, Sc = O.gated_scan(q64[:, :, :64 * c], k64[:, :, :64 * c], v64[:, :, :64 * c],
                              f64[:, :, :64 * c], S0=S0.double().numpy(), return_final=True)
         assert rel_max_err(seg[:, :, c].float().cpu().numpy(), Sc) <= TOL_BF16
+
+
+def test_resume_refused_without_matching_state_only_pass(mg):
+    """A resumed output pass needs the chunk-local states of the same k, v, f
+    in the workspace: after a call that kept its states elsewhere
+    (save_states) or after a forward of other inputs it is refused."""
+    from mogt_b200 import ops
+    q, k, v, f = (t.cuda() for t in headed_bf16(1, 2, 700, seed=31))
+    ops.gated_scan_fwd(q, k, v, f, save_states=True)
+    with pytest.raises(ValueError, match="resume"):
+        ops.gated_scan_fwd(q, k, v, f, resume=True)
+    ops.gated_scan_fwd(None, k, v, f, want_final=True, want_output=False)
+    k2 = k.clone()
+    with pytest.raises(ValueError, match="resume"):
+        ops.gated_scan_fwd(q, k2, v, f, resume=True)
+    o, _, _, _ = ops.gated_scan_fwd(q, k, v, f, resume=True)
+    assert torch.equal(o, ops.gated_scan_fwd(q, k, v, f)[0])
