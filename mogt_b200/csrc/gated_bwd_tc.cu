@@ -68,7 +68,7 @@ constexpr int SM_ROWK = SM_ROWY + 512;             // [2][64] halves of k.(M1d^T
 constexpr int SM_COLW = SM_ROWK + 512;             // [4][64] column sums of the E prefix
 constexpr int SM_ROWT = SM_COLW + 1024;            // [64] row totals of E, columns 0..31
 constexpr int SM_SIG = SM_ROWT + 256;              // [8] <X, S_in> per warp
-constexpr int SM_MISC = SM_ROWZ + 2 * PART;        // ticket, look-back scratch
+constexpr int SM_MISC = SM_ROWZ + 2 * PART;        // ticket, epoch
 constexpr int NBARS = STAGES + 5;
 constexpr int SM_BAR = SM_MISC + 256;
 constexpr int SM_TSLOT = SM_BAR + 8 * NBARS;
@@ -91,10 +91,10 @@ struct Params {
   float* df;
   float* dS0;
   WsHeader* hdr;
-  // when set: the carry entering every stripe's end comes from the segment
-  // passes (gated_bwd_seg_agg + the segment carry), [BH][nseg_b][4096] in the
-  // stripe-aggregate layout, segments in reverse time order; pass 1 and the
-  // look-back are skipped
+  // the carry entering every stripe's end, from the segment passes
+  // (gated_bwd_seg_agg + the segment carry): [BH][nseg_b][4096] in the
+  // fragment-register order of the 8-warp layout, segments in reverse time
+  // order, nsub segments per stripe
   const float* x_in;
   int nseg_b, nsub;
   int T, BH, nchunks, cps, nstripes;
@@ -585,7 +585,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
 // gated_bwd_seg_agg: the backward carry's aggregate over a segment of chunks
 // (a third of a stripe), sum_c exp2(lpre_c) (diag(exp2 l) Q_c)^T dO_c with
 // lpre_c the log2 decay of the segment's chunks before c, and the segment's
-// total log2 decay: the quantities pass 1 forms per stripe, here with three
+// total log2 decay, with three
 // light CTAs per SM and one accumulator in tensor memory.  Written in reverse
 // segment order, so that the forward's segment carry kernel run over them
 // gives the carry entering each segment's end from the later ones.
@@ -712,7 +712,7 @@ using namespace mogt::gated;
 namespace mogt {
 namespace gated {
 
-// The stripe kernel's look-back workspace, then the segment aggregates, log2
+// The 256-byte header (ticket, epoch, sticky error), then the segment aggregates, log2
 // decays and carries of the segment passes (bwd::kSub segments per stripe).
 namespace bwd {
 constexpr int kSub = 3;
@@ -773,8 +773,7 @@ int launch_bwd_tc(const void* q, const void* k, const void* v, const float* f, c
   P.cps = pl.cps;
   P.nstripes = pl.nstripes;
   // the carry entering every stripe's end: segment aggregates (three light
-  // CTAs per SM) and the segment carry, instead of the stripe kernel's pass 1
-  // and look-back
+  // CTAs per SM) and the segment carry
   bwd::AggParams A;
   A.f = f;
   A.agg = reinterpret_cast<float*>(ws + SL.agg);
